@@ -1,0 +1,408 @@
+"""Decode benchmark of the B200 backend on the Qwen2-1.5B architecture.
+
+Headline (`value`): greedy batch-1 decode tok/s of the full 28-layer
+Qwen2-1.5B architecture in bf16 (random weights, 512-token prompt), one
+request per GPU; with N GPUs every rank decodes its own request on its own
+model replica (requests partitioned across GPUs, no collective on the data
+path), so `value` is the whole-box tok/s and scaling is weak. A step is one
+decode token: one CUDA-graph launch of the 28-layer step with the token
+buffer on the device. Weights (3.1 GB) exceed L2 (126 MB), so no flush is
+needed between steps.
+
+`e2e`: the same metric through the public call a user makes
+(wgb_qwen2_infer: host token in, host token out), with the 8-byte
+host->device and device->host copies inside the timed region.
+
+Extra objects: `bs64` (64 sequences with 2048-token prompts on the
+one-layer model, requests split across the GPUs), `roofline` (the weight-
+streaming GEMV, the dominant kernel), `cpu_baseline` (the reference's own CPU
+build timed on a bounded sample), `clocks`.
+
+`--impl reference` times the reference's own CPU implementation
+(oracle/_ref) on the host cores for the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s (Qwen2-1.5B arch bf16, bs1 & bs64) + per-op HBM GB/s vs peak"
+UNIT = "tok/s"
+
+
+def load_peaks():
+    try:
+        p = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------- helpers
+def dist_setup(n_gpus):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def device_weights(cfg, seed, device):
+    """Random weights drawn on the device (same distributions as
+    wginfer_b200.synthetic, a device generator stream)."""
+    import torch
+    from wginfer_b200.synthetic import LAYER_NAMES
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def draw(shape, std, mean=0.0):
+        t = torch.randn(shape, generator=g, device=device, dtype=torch.float32)
+        t.mul_(std).add_(mean)
+        return t.to(cfg.dtype)
+
+    w = {"in_embed": draw((cfg.voc, cfg.hs), 0.02)}
+    shapes = cfg.shapes()
+    for n in LAYER_NAMES:
+        w[n] = []
+    for _ in range(cfg.nlayer):
+        for n in LAYER_NAMES:
+            w[n].append(draw(shapes[n], 0.1, 1.0) if n.endswith("norm_w") else draw(shapes[n], 0.02))
+    w["out_norm_w"] = draw((cfg.hs,), 0.1, 1.0)
+    w["out_embed"] = draw((cfg.voc, cfg.hs), 0.02)
+    return w
+
+
+def build_model(cfg, max_batch, device_index, seed=0, keep=()):
+    import torch
+    from wginfer_b200.qwen2 import Qwen2
+    dev = torch.device("cuda", device_index)
+    w = device_weights(cfg, seed, dev)
+    m = Qwen2(cfg, None, device=device_index, max_batch=max_batch)
+    m.load_weights(w)
+    kept = {k: w[k] for k in keep}
+    del w
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    return m, kept
+
+
+# ---------------------------------------------------------------- B200 arm
+def time_decode(m, batch, K, W, world):
+    import torch
+    s = m.torch_stream()
+    for _ in range(W):
+        m.decode_step(batch)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(K):
+        m.decode_step(batch)
+    e1.record(s)
+    e1.synchronize()
+    barrier(world)
+    return e0.elapsed_time(e1) / 1e3
+
+
+def gemv_roofline(w_out, hs, voc, peak, K=20):
+    """Times the lm_head GEMV (the largest weight-streaming launch, [1,1536] x
+    [151936,1536]^T) live with CUDA events on the launching stream."""
+    import torch
+    from wginfer_b200 import numerics, ops
+    x = torch.randn(1, hs, device=w_out.device).to(w_out.dtype)
+    out = torch.empty(1, voc, device=w_out.device, dtype=w_out.dtype)
+    with numerics("fast"):
+        for _ in range(3):
+            ops.linear(out, x, w_out)
+        s = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(K):
+            ops.linear(out, x, w_out)
+        e1.record(s)
+        e1.synchronize()
+    dt = e0.elapsed_time(e1) / 1e3 / K
+    nbytes = (voc * hs + hs + voc) * w_out.element_size()
+    achieved = nbytes / dt / 1e9
+    traffic = None
+    try:
+        prof = json.load(open(os.path.join(ROOT, "profiles", "gemv_lm_head_traffic.json")))
+        traffic = prof.get("dram_bytes_per_launch")
+    except Exception:
+        pass
+    return {"kernel": "gemv_kernel (lm_head [1,1536]x[151936,1536]^T, bf16)", "bound": "hbm",
+            "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "traffic": traffic, "algorithmic_bytes": nbytes, "us_per_launch": round(dt * 1e6, 2)}
+
+
+def run_b200(args):
+    import torch
+    from wginfer_b200 import numerics
+    from wginfer_b200.synthetic import Qwen2Config, prompt_ids
+
+    world, rank, local = dist_setup(args.gpus)
+    peak, peak_src = load_peaks()
+    K, W = args.steps, args.warmup
+    maxseq = args.prompt + W + K + W + K + 8
+    cfg = Qwen2Config(nlayer=28, maxseq=maxseq)
+    result = {"metric": METRIC, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+              "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+              "data": "synthetic (seeded random weights ~N(0,0.02), uniform random prompt ids)"}
+    with numerics(args.numerics):
+        m, kept = build_model(cfg, 1, local, seed=0, keep=("out_embed",))
+        m.prefill(0, prompt_ids(args.prompt, cfg.voc, seed=rank).numpy())
+        with Clocks(local) as clk:
+            t = time_decode(m, 1, K, W, world)
+        t_max = max_over_ranks(t, world)
+        value = world * K / t_max
+        # e2e through the public API: host token in, host token out, every step
+        s = m.torch_stream()
+        tok = m.tokens(1)[0]
+        for _ in range(W):
+            tok = m.infer([tok])
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(K):
+            tok = m.infer([tok])
+        e1.record(s)
+        e1.synchronize()
+        barrier(world)
+        te = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
+        roof = gemv_roofline(kept["out_embed"], cfg.hs, cfg.voc, peak)
+        roof["peak_source"] = peak_src
+        del kept
+        m.close()
+        torch.cuda.empty_cache()
+    bytes_per_token = cfg.weight_bytes()
+    result.update({
+        "value": round(value, 2), "ms_per_step": round(t_max / K * 1e3, 4),
+        "config": {"workload": "Qwen2-1.5B arch (28 layers, hidden 1536, 12/2 heads x 128, MLP 8960, vocab "
+                               "151936), greedy decode, batch 1 per GPU, prompt %d" % args.prompt,
+                   "global_batch": world, "seq_len": args.prompt + K, "parallelism": f"replicas x{world}",
+                   "numerics": args.numerics, "l2": "weights 3.1 GB > L2; no flush needed"},
+        "weight_stream_roofline": {"bytes_per_token": bytes_per_token,
+                                   "tok_s_at_peak": round(peak * 1e9 / bytes_per_token, 1),
+                                   "frac": round(value / world / (peak * 1e9 / bytes_per_token), 4)},
+        "e2e": {"value": round(world * K / te, 2), "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
+        "roofline": roof,
+        "clocks": clk.summary(),
+        # per step: embedding, 28 x (rms_norm, qkv gemv, qkv_post, attention split + combine, o gemv,
+        # rms_norm, gate/up gemv, swiglu, down gemv), final rms_norm, lm_head gemv, argmax, 2 bookkeeping
+        "gpu_launches": K * (1 + 28 * 10 + 3 + 2 + 1),
+    })
+    if not args.no_bs64:
+        result["bs64"] = bs64(args, world, rank, local)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def bs64(args, world, rank, local):
+    """64 sequences x 2048-token prompts, 256-token decode budget, on the
+    one-layer model; each GPU holds 64/N of them."""
+    from wginfer_b200 import numerics
+    from wginfer_b200.synthetic import Qwen2Config, prompt_ids
+    total = 64
+    per = total // world
+    K, W = min(args.steps, 200), min(args.warmup, 8)
+    cfg = Qwen2Config(nlayer=1, maxseq=2048 + 256)
+    with numerics(args.numerics):
+        m, _ = build_model(cfg, per, local, seed=0)
+        ids = prompt_ids(2048, cfg.voc, seed=1000, batch=total).numpy()
+        t0 = time.time()
+        for b in range(per):
+            m.prefill(b, ids[rank * per + b])
+        prefill_s = time.time() - t0
+        t = time_decode(m, per, K, W, world)
+        m.close()
+    t_max = max_over_ranks(t, world)
+    return {"value": round(total * K / t_max, 1), "unit": UNIT, "sequences": total, "per_gpu": per,
+            "prompt": 2048, "steps": K, "ms_per_step": round(t_max / K * 1e3, 4), "scaling": "strong",
+            "prefill_s_rank0": round(prefill_s, 2),
+            "workload": "one-layer Qwen2 (config-2 layer + embeddings + lm_head), bf16, greedy"}
+
+
+# ---------------------------------------------------------------- reference CPU arm
+def reference_decode_sample(budget_s: float, steps: int | None = None, warmup: int = 1):
+    """The reference's Model::infer (oracle/_ref) on the host cores, one
+    decode token per step on 1- and 2-layer models of the full dimensions;
+    the full 28-layer token time is extrapolated as t1 + 27 (t2 - t1)."""
+    import numpy as np
+    from oracle import oracle as O
+    from tests.golden import cases as CS
+    from wginfer_b200.synthetic import Qwen2Config
+    ref = O.Reference()
+    models = []
+    for nl in (1, 2):
+        cfg = Qwen2Config(nlayer=nl, maxseq=64)
+        meta, w = CS.model_inputs(cfg, seed=0)
+        m = O.ReferenceQwen2(ref, meta, w)
+        m.infer(np.array([1], np.int64))
+        models.append((m, w))
+    per_token = []
+    t_start = time.time()
+    n = 0
+    while True:
+        t1s = time.perf_counter()
+        models[0][0].infer(np.array([2], np.int64))
+        t1 = time.perf_counter() - t1s
+        t2s = time.perf_counter()
+        models[1][0].infer(np.array([2], np.int64))
+        t2 = time.perf_counter() - t2s
+        n += 1
+        if n > warmup:
+            per_token.append(t1 + 27 * max(t2 - t1, 0.0))
+        if steps is not None and n >= steps + warmup:
+            break
+        if steps is None and time.time() - t_start > budget_s and per_token:
+            break
+    return per_token
+
+
+def cpu_baseline(budget_s):
+    try:
+        from oracle import oracle as O
+        if not os.path.exists(O.REF_SO):
+            return {"value": None, "unavailable": "oracle/_ref not built"}
+        per = reference_decode_sample(budget_s, warmup=0)
+        v = 1.0 / statistics.median(per)
+        return {"value": round(v, 4), "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+                "sample": f"{len(per)} decode tokens of the reference Model on 1- and 2-layer models of the "
+                          "full dimensions (batch 1; its linear is single-threaded below 64 rows), 28-layer "
+                          "time extrapolated as t1 + 27 (t2 - t1)"}
+    except Exception as e:  # reported, never fatal for the GPU arm
+        return {"value": None, "unavailable": f"{type(e).__name__}: {e}"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    if not os.path.exists(O.REF_SO):
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (reference CPU build) missing"}))
+        return
+    # bound the whole run to a few minutes: cap the number of sampled tokens
+    steps = max(1, min(args.steps, args.ref_max_steps))
+    per = reference_decode_sample(0, steps=steps, warmup=min(args.warmup, 1))
+    t = sum(per)
+    value = len(per) / t
+    cores = os.cpu_count()
+    out = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+           "steps": len(per), "warmup": min(args.warmup, 1), "ms_per_step": round(t / len(per) * 1e3, 2),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (seeded random weights)",
+           "config": {"workload": "Qwen2-1.5B arch greedy decode, batch 1 (reference Model::infer on the CPU "
+                                  "device)", "global_batch": 1, "seq_len": 2, "parallelism": "none"},
+           "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "reference",
+                            "sample": "per step one decode token on 1- and 2-layer reference models of the full "
+                                      "dimensions; 28-layer time = t1 + 27 (t2 - t1)"},
+           "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--numerics", default="fast", choices=["fast", "reference"])
+    ap.add_argument("--no-bs64", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--ref-max-steps", type=int, default=12)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

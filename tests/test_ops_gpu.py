@@ -1,0 +1,187 @@
+"""Parity of every op with the CPU oracle on the seeded cases, through the
+C-ABI. REFERENCE numerics must be bit-identical (f16 within one f16 ulp:
+the reference's CPU f16 conversion truncates where the device rounds to
+nearest); FAST numerics within the tolerances the backend promises:
+1e-5 relative for f32, 2e-2 relative for bf16/f16 (atol 1e-2), exact for
+add, embedding and argmax."""
+import numpy as np
+import pytest
+import torch
+
+from tests.golden import cases as CS
+from wginfer_b200 import numerics, ops
+
+pytestmark = pytest.mark.gpu
+
+EXACT_OPS = {"add", "embedding", "argmax"}
+
+
+def as_f32(a):
+    if a.dtype == np.float32 or a.dtype == np.int64:
+        return a.astype(np.float64)
+    return (a.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+
+
+def f16_f64(a):
+    return a.view(np.float16).astype(np.float64)
+
+
+@pytest.fixture(scope="module")
+def gpu(cuda):
+    from tests.gpu_runner import Gpu
+    return Gpu()
+
+
+@pytest.mark.parametrize("mode", ["reference", "fast"])
+@pytest.mark.parametrize("cid", range(len(CS.OP_CASES)))
+def test_op_parity(oracle, gpu, mode, cid):
+    case = CS.OP_CASES[cid]
+    ins = CS.inputs(case)
+    want = CS.run_case(oracle, case, ins)
+    with numerics(mode):
+        got = CS.run_case(gpu, case, ins)
+    torch.cuda.synchronize()
+    for g, w in zip(got, want):
+        if case["dtype"] == "f16" and case["op"] not in ("embedding",):
+            if case["op"] == "argmax":
+                assert np.array_equal(g, w)
+                continue
+            # device rounds to nearest, the reference's CPU f16 conversion truncates
+            np.testing.assert_allclose(f16_f64(g), f16_f64(w), rtol=2e-3 if mode == "reference" else 2e-2, atol=1e-3)
+            continue
+        if mode == "reference" or case["op"] in EXACT_OPS:
+            assert np.array_equal(g, w), f"{case}: max diff {np.abs(as_f32(g) - as_f32(w)).max()}"
+        elif case["dtype"] == "f32":
+            np.testing.assert_allclose(as_f32(g), as_f32(w), rtol=1e-5, atol=1e-5)
+        else:
+            np.testing.assert_allclose(as_f32(g), as_f32(w), rtol=2e-2, atol=1e-2)
+
+
+def _bf16(shape, seed, std=1.0, mean=0.0):
+    g = torch.Generator("cpu").manual_seed(seed)
+    return (torch.randn(shape, generator=g) * std + mean).to(torch.bfloat16).cuda()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("n", [(1 << 25) + 3, 64 << 20])
+def test_add_swiglu_large_vs_torch(cuda, dtype, n):
+    g = torch.Generator("cpu").manual_seed(n % 1000)
+    a = torch.randn(n, generator=g).to(dtype).cuda()
+    b = torch.randn(n, generator=g).to(dtype).cuda()
+    c = torch.empty_like(a)
+    ops.add(c, a, b)
+    assert torch.equal(c, (a.float() + b.float()).to(dtype))
+    o = torch.empty_like(a).view(1, -1)
+    ops.swiglu(o, a.view(1, -1), b.view(1, -1))
+    ref = (b.float() * a.float() / (1 + torch.exp(-a.float()))).to(dtype)
+    torch.testing.assert_close(o.view(-1).float(), ref.float(), rtol=2e-2 if dtype != torch.float32 else 1e-5,
+                               atol=1e-2 if dtype != torch.float32 else 1e-5)
+
+
+@pytest.mark.parametrize("N", [1536, 4096, 8192, 1000])
+def test_rms_norm_large_vs_torch(cuda, N):
+    M = (64 << 20) // (2 * N)
+    x = _bf16((M, N), N)
+    w = _bf16((N,), N + 1, 0.1, 1.0)
+    out = torch.empty_like(x)
+    ops.rms_norm(out, x, w, 1e-6)
+    xf = x.float()
+    ref = (xf * w.float() * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+    torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("B", [1, 3, 64, 256])
+def test_argmax_rows_first_index(oracle, cuda, B):
+    V = 151936
+    vals = _bf16((B, V), B)
+    # plant ties: copy each row's max to an earlier and a later position
+    am = vals.float().argmax(-1)
+    for r in range(B):
+        vals[r, 7] = vals[r, am[r]]
+        vals[r, V - 1] = vals[r, am[r]]
+    idx = torch.empty(B, dtype=torch.int64, device="cuda")
+    val = torch.empty(B, dtype=torch.bfloat16, device="cuda")
+    ops.argmax_rows(idx, val, vals)
+    host = vals.cpu().view(torch.int16).numpy().view(np.uint16)
+    vh = val.cpu().view(torch.int16).numpy().view(np.uint16)
+    for r in range(B):
+        i, v = oracle.argmax(np.ascontiguousarray(host[r]), 15)
+        assert idx[r].item() == i and vh[r] == v
+
+
+def test_argmax_nan_semantics(oracle, cuda):
+    v = torch.tensor([float("nan"), 1.0, 3.0, 2.0], device="cuda")
+    idx = torch.zeros(1, dtype=torch.int64, device="cuda")
+    val = torch.zeros(1, device="cuda")
+    ops.argmax(idx, val, v)
+    assert idx.item() == 0  # the sequential scan keeps a NaN at index 0
+    v = torch.tensor([1.0, float("nan"), 3.0, 3.0, -0.0], device="cuda")
+    ops.argmax(idx, val, v)
+    assert idx.item() == 2 and val.item() == 3.0
+
+
+def test_embedding_out_of_range_is_recorded(cuda):
+    w = _bf16((16, 64), 9)
+    out = torch.full((3, 64), 7.0, dtype=torch.bfloat16, device="cuda")
+    idx = torch.tensor([1, 16, 2], device="cuda")
+    ops.device_error()  # clear
+    ops.embedding(out, idx, w)
+    code, value = ops.device_error()
+    assert code == 1 and value == 16
+    assert torch.equal(out[0], w[1]) and torch.equal(out[2], w[2]) and torch.all(out[1] == 0)
+    assert ops.device_error() == (0, 0)
+
+
+def test_rope_in_place_and_unaligned_views(oracle, cuda):
+    x = _bf16((4 * 12 * 128 + 1,), 3)
+    view = x[1:].view(4, 12, 128)  # 2-byte offset: not 16-byte aligned
+    pos = torch.arange(10, 14, device="cuda")
+    want = torch.empty_like(view)
+    ops.rope(want, view.clone(), pos, 1e4)
+    ops.rope(view, view, pos, 1e4)  # in place
+    assert torch.equal(view, want)
+    a, b = _bf16((1001,), 4), _bf16((1001,), 5)
+    c = torch.empty(1002, dtype=torch.bfloat16, device="cuda")
+    ops.add(c[1:], a, b)
+    assert torch.equal(c[1:], (a.float() + b.float()).to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("mode", ["fast", "reference"])
+def test_linear_unaligned_and_ragged(oracle, cuda, mode):
+    M, N, K = 3, 50, 77
+    x, w, b = _bf16((M, K), 1), _bf16((N, K), 2, 0.02), _bf16((N,), 3, 0.02)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    with numerics(mode):
+        ops.linear(out, x, w, b)
+    h = lambda t: t.cpu().view(torch.int16).numpy().view(np.uint16)
+    want = np.zeros((M, N), np.uint16)
+    oracle.linear(want, h(x), h(w), h(b), 15)
+    got = h(out)
+    if mode == "reference":
+        assert np.array_equal(got, want)
+    else:
+        np.testing.assert_allclose(as_f32(got), as_f32(want), rtol=2e-2, atol=1e-2)
+
+
+def test_attention_workspace_contract(cuda):
+    import ctypes as C
+    from wginfer_b200 import _lib
+    l = _lib.lib()
+    need = l.wgb_self_attention_workspace_size(1, 12, 2, 128, 128, 4096)
+    assert need > 0
+    q = _bf16((1, 12, 128), 1)
+    k = _bf16((4096, 2, 128), 2)
+    v = _bf16((4096, 2, 128), 3)
+    out = torch.empty_like(q)
+    p = lambda t: C.c_void_p(t.data_ptr())
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = l.wgb_self_attention_ex(p(out), p(q), p(k), p(v), 15, 1, 12, 2, 128, 128, 4096, C.c_float(0.088), None, 0, st)
+    assert rc == 1
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    rc = l.wgb_self_attention_ex(p(out), p(q), p(k), p(v), 15, 1, 12, 2, 128, 128, 4096, C.c_float(0.088), p(ws),
+                                 need, st)
+    assert rc == 0
+    out2 = torch.empty_like(q)
+    ops.self_attention(out2, q, k, v, 0.088)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)

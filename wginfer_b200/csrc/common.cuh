@@ -1,0 +1,121 @@
+// Shared device helpers for the sm_100a decode-path kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "wginfer_b200.h"
+
+namespace wgb {
+
+constexpr int kNumSMs = 148;  // B200: 2 dies x 74 SMs (queried at run time too)
+
+// ---- element types -------------------------------------------------------
+// Stores round to nearest even (bf16, f16). For finite values the bf16 result
+// equals the reference's host conversion (utils/types.cpp:74-83).
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+    static __device__ __forceinline__ float load(float v) { return v; }
+    static __device__ __forceinline__ float store(float v) { return v; }
+};
+template <> struct Elem<__nv_bfloat16> {
+    static __device__ __forceinline__ float load(__nv_bfloat16 v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ __nv_bfloat16 store(float v) { return __float2bfloat16_rn(v); }
+};
+template <> struct Elem<__half> {
+    static __device__ __forceinline__ float load(__half v) { return __half2float(v); }
+    static __device__ __forceinline__ __half store(float v) { return __float2half_rn(v); }
+};
+
+template <typename T> __device__ __forceinline__ float ldf(const T *p, size_t i) {
+    return Elem<T>::load(p[i]);
+}
+template <typename T> __device__ __forceinline__ void stf(T *p, size_t i, float v) {
+    p[i] = Elem<T>::store(v);
+}
+
+// 16-byte vector of T.
+template <typename T> struct Vec16 {
+    static constexpr int N = 16 / sizeof(T);
+    union {
+        uint4 u;
+        T e[N];
+    };
+};
+
+__device__ __forceinline__ uint4 ld_global_nc_v4(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+// Streaming load for data read exactly once (weights): evict-first in L2,
+// expressed as an L2 cache-policy operand.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ uint4 ld_stream_v4(const void *p, uint64_t pol) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p), "l"(pol));
+    return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Correctly rounded (with overwhelming probability) single-precision
+// transcendentals evaluated in double precision. Used where results must
+// agree with a correctly rounding C library.
+__device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
+__device__ __forceinline__ float sin_cr(float x) { return (float)sin((double)x); }
+__device__ __forceinline__ float cos_cr(float x) { return (float)cos((double)x); }
+__device__ __forceinline__ float pow_cr(float b, float e) { return (float)pow((double)b, (double)e); }
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Records the first bad value a kernel met ({code, value}) in the library's
+// device error word (status.cu) instead of faulting.
+__device__ __forceinline__ void record_device_error(unsigned long long *rec, int code, long long value) {
+    if (rec != nullptr && atomicCAS(rec, 0ull, (unsigned long long)code) == 0ull)
+        rec[1] = (unsigned long long)value;
+}
+
+}  // namespace wgb
+
+// ---- host-side status plumbing (status.cpp) --------------------------------
+namespace wgb {
+int set_error(int status, const char *fmt, ...);
+int check_launch(const char *what);
+int current_numerics();
+int sm_count();
+unsigned long long *dev_error_ptr();
+}  // namespace wgb
+
+#define WGB_REQUIRE(cond, status, ...)                    \
+    do {                                                  \
+        if (!(cond)) return ::wgb::set_error(status, __VA_ARGS__); \
+    } while (0)
+
+#define WGB_DISPATCH_FLOAT(dtype, T, ...)                                                    \
+    switch (dtype) {                                                                         \
+    case WGINFER_DTYPE_F32: { using T = float; __VA_ARGS__; break; }                         \
+    case WGINFER_DTYPE_BF16: { using T = __nv_bfloat16; __VA_ARGS__; break; }                \
+    case WGINFER_DTYPE_F16: { using T = __half; __VA_ARGS__; break; }                        \
+    default:                                                                                 \
+        return ::wgb::set_error(WGB_ERR_UNSUPPORTED_DTYPE, "unsupported dtype %d", (int)dtype); \
+    }

@@ -1,0 +1,631 @@
+// Qwen2 decoder on the B200 backend: the caller of the decode-path ops.
+//
+// Follows src/models/qwen2/model.cpp (forward_layer :243-328, forward
+// :331-368, infer :371-415) with the same op sequence and rounding points,
+// re-planned for the device:
+//  - one device arena holds weights, per-sequence KV caches and activations;
+//  - q/k/v weights (and biases) are stored as one [(nh + 2 nkvh) dh, hs]
+//    matrix and gate/up as one [2 di, hs] matrix, so each is one GEMV; each
+//    output row is still its own dot product, so results are unchanged;
+//  - RoPE, the K/V cache append (the reference's two synchronous D2D copies)
+//    and the q copy are one kernel reading a cos/sin table built on the host
+//    with the reference's exact formula (rope_cpu.cpp:13-30);
+//  - the residual adds are fused into the o_proj and down_proj epilogues
+//    (round(x + round(W a)), the reference's linear-then-add);
+//  - logits are formed for the last prompt row only (the reference computes
+//    every row and reads the last, model.cpp:363-396);
+//  - greedy argmax stays on the device; a decode step for a batch of
+//    sequences reads and writes a device token buffer and is captured once
+//    into a CUDA graph, so a step costs one graph launch and no host sync.
+#include <cmath>
+#include <cstring>
+#include <algorithm>
+#include <numeric>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace wgb {
+namespace {
+
+size_t dsize(int dt) { return dt == WGINFER_DTYPE_F32 ? 4 : 2; }
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// qkv rows [T, (nh + 2 nkvh) * dh] -> q_rope [T, nh, dh] and, for the k/v
+// heads, the cache of sequence seq(t) at position pos[t]. One thread per
+// rotation pair (j, j + dh/2) per head.
+template <typename T>
+__global__ void __launch_bounds__(128) qkv_post_kernel(const T *__restrict__ qkv, T *__restrict__ q_out, T *kcache,
+                                                       T *vcache, const int64_t *__restrict__ pos,
+                                                       const float2 *__restrict__ table, int T_rows, int nh,
+                                                       int nkvh, int dh, int maxseq, int prefill_seq,
+                                                       size_t seq_stride, unsigned long long *err) {
+    const int t = blockIdx.y;
+    const int half = dh / 2;
+    const int nq = nh + 2 * nkvh;
+    int64_t p = pos[t];
+    if (p < 0 || p >= maxseq) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) record_device_error(err, 3, p);
+        return;
+    }
+    const int seq = prefill_seq >= 0 ? prefill_seq : t;
+    const T *row = qkv + (size_t)t * nq * dh;
+    T *kc = kcache + (size_t)seq * seq_stride + (size_t)p * nkvh * dh;
+    T *vc = vcache + (size_t)seq * seq_stride + (size_t)p * nkvh * dh;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < (nh + nkvh) * half + nkvh * dh;
+         idx += gridDim.x * blockDim.x) {
+        if (idx < (nh + nkvh) * half) {
+            const int h = idx / half, j = idx - h * half;  // h < nh: q head; else k head h - nh
+            const float2 cs = table[(size_t)p * half + j];
+            const T *src = row + (size_t)h * dh;
+            const float a = ldf(src, j), b = ldf(src, j + half);
+            const float o0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+            const float o1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+            T *dst = h < nh ? q_out + ((size_t)t * nh + h) * dh : kc + (size_t)(h - nh) * dh;
+            stf(dst, j, o0);
+            stf(dst, j + half, o1);
+        } else {
+            const int e = idx - (nh + nkvh) * half;  // v element
+            vc[e] = row[(size_t)(nh + nkvh) * dh + e];
+        }
+    }
+}
+
+// act[t, j] = swiglu(gu[t, j], gu[t, di + j]) (swiglu_cpu.cpp:11).
+template <typename T, bool kRef>
+__global__ void __launch_bounds__(256) swiglu_rows_kernel(T *__restrict__ act, const T *__restrict__ gu, int T_rows,
+                                                          int di) {
+    const size_t n = (size_t)T_rows * di;
+    for (size_t i = (size_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (size_t)gridDim.x * 256) {
+        const size_t t = i / di, j = i - t * di;
+        const float g = ldf(gu, t * 2 * di + j), u = ldf(gu, t * 2 * di + di + j);
+        const float e = kRef ? exp_cr(-g) : expf(-g);
+        stf(act, i, __fdiv_rn(__fmul_rn(u, g), __fadd_rn(1.0f, e)));
+    }
+}
+
+__global__ void fill_positions_kernel(int64_t *pos, int64_t start, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) pos[i] = start + i;
+}
+
+__global__ void decode_begin_kernel(int64_t *pos, const int64_t *lens, int B) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) pos[b] = lens[b];
+}
+
+__global__ void decode_end_kernel(int64_t *lens, int B, int maxseq) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B && lens[b] < maxseq) lens[b] += 1;
+}
+
+int64_t argmax_host(const std::vector<float> &v) {
+    size_t best = 0;
+    for (size_t i = 1; i < v.size(); ++i)
+        if (v[i] > v[best]) best = i;
+    return (int64_t)best;
+}
+
+// Host sampling, the reference's sample_from_logits (model.cpp:60-137).
+int64_t sample_host(const std::vector<float> &logits, int top_k, float top_p, float temperature) {
+    if (temperature <= 0.0f) return argmax_host(logits);
+    const size_t vocab = logits.size();
+    if (top_k <= 0 || top_k > (int)vocab) top_k = (int)vocab;
+    if (top_p <= 0.0f || top_p > 1.0f) top_p = 1.0f;
+    if (top_k == 1 && top_p >= 1.0f) return argmax_host(logits);
+    std::vector<int> idx(vocab);
+    std::iota(idx.begin(), idx.end(), 0);
+    auto desc = [&logits](int a, int b) { return logits[a] > logits[b]; };
+    if (top_k < (int)vocab) {
+        std::partial_sort(idx.begin(), idx.begin() + top_k, idx.end(), desc);
+        idx.resize(top_k);
+    } else {
+        std::sort(idx.begin(), idx.end(), desc);
+    }
+    const float inv_t = 1.0f / temperature;
+    float mx = -INFINITY;
+    for (int i : idx) mx = std::max(mx, logits[i] * inv_t);
+    std::vector<double> probs(idx.size());
+    double total = 0.0;
+    for (size_t i = 0; i < idx.size(); ++i) {
+        double p = std::exp((double)(logits[idx[i]] * inv_t - mx));
+        if (!std::isfinite(p) || p < 0.0) p = 0.0;
+        probs[i] = p;
+        total += p;
+    }
+    if (total <= 0.0) return idx.front();
+    if (top_p < 1.0f) {
+        double cum = 0.0;
+        size_t keep = 0;
+        for (size_t i = 0; i < probs.size(); ++i) {
+            cum += probs[i] / total;
+            keep = i + 1;
+            if (cum >= (double)top_p) break;
+        }
+        keep = std::max<size_t>(keep, 1);
+        idx.resize(keep);
+        probs.resize(keep);
+    }
+    thread_local std::mt19937 rng(std::random_device{}());
+    std::discrete_distribution<int> dist(probs.begin(), probs.end());
+    return idx[(size_t)dist(rng)];
+}
+
+}  // namespace
+}  // namespace wgb
+
+using namespace wgb;
+
+struct LayerW {
+    void *attn_norm, *qkv_w, *qkv_b, *o_w, *mlp_norm, *gu_w, *down_w;
+};
+
+struct wgbQwen2Model {
+    wgbQwen2Meta m;
+    int device = 0, max_batch = 1, chunk = 1;
+    wginferDataType_t dt;
+    size_t es = 2;
+    cudaStream_t stream = nullptr;
+    char *arena = nullptr;
+    size_t arena_bytes = 0;
+    // weights
+    void *in_embed, *out_embed, *out_norm;
+    std::vector<LayerW> L;
+    float2 *rope_table;
+    // caches and state
+    void *kc, *vc;
+    size_t seq_stride;  // elements per sequence per layer in kc / vc
+    int64_t *lens, *tokens, *pos;
+    // activations (rows = max(max_batch, chunk))
+    void *x, *xn, *qkv, *qr, *att, *gu, *act, *logits;
+    void *attn_ws;
+    size_t attn_ws_bytes;
+    int64_t *h_pinned;  // pinned host staging for token ids
+    size_t h_pinned_n;
+    std::vector<size_t> h_lens;
+    std::vector<bool> has_bias;
+    // graphs per (batch, numerics)
+    std::vector<cudaGraphExec_t> graphs[2];
+
+    size_t nq() const { return (m.nh + 2 * m.nkvh) * m.dh; }
+    void *layer_k(size_t l) const { return (char *)kc + l * max_batch * seq_stride * es; }
+    void *layer_v(size_t l) const { return (char *)vc + l * max_batch * seq_stride * es; }
+};
+
+namespace {
+
+int cuda_err(const char *what) { return check_launch(what); }
+
+// One transformer layer over T rows (model.cpp:243-328).
+int run_layer(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t total_len, bool ref) {
+    const wgbQwen2Meta &m = M->m;
+    cudaStream_t s = M->stream;
+    const LayerW &w = M->L[l];
+    const int hs = (int)m.hs, di = (int)m.di;
+    int rc;
+    if ((rc = wgb_rms_norm(M->xn, M->x, w.attn_norm, M->dt, T, hs, m.epsilon, s))) return rc;
+    if ((rc = linear_forward(M->dt, M->qkv, M->xn, w.qkv_w, w.qkv_b, nullptr, T, (int)M->nq(), hs, ref, s))) return rc;
+    {
+        const int half = (int)m.dh / 2;
+        const int work = (int)((m.nh + m.nkvh) * half + m.nkvh * m.dh);
+        dim3 grid((unsigned)((work + 127) / 128), (unsigned)T);
+        WGB_DISPATCH_FLOAT(M->dt, Tt,
+            qkv_post_kernel<Tt><<<grid, 128, 0, s>>>((const Tt *)M->qkv, (Tt *)M->qr, (Tt *)M->layer_k(l),
+                                                     (Tt *)M->layer_v(l), M->pos, M->rope_table, T, (int)m.nh,
+                                                     (int)m.nkvh, (int)m.dh, (int)m.maxseq, prefill_seq,
+                                                     M->seq_stride, dev_error_ptr()));
+        if ((rc = cuda_err("qkv_post"))) return rc;
+    }
+    const float scale = 1.0f / sqrtf((float)m.dh);
+    if (prefill_seq >= 0) {
+        const char *kb = (const char *)M->layer_k(l) + (size_t)prefill_seq * M->seq_stride * M->es;
+        const char *vb = (const char *)M->layer_v(l) + (size_t)prefill_seq * M->seq_stride * M->es;
+        int prev = wgb_get_numerics();
+        wgb_set_numerics(ref ? WGB_NUMERICS_REFERENCE : WGB_NUMERICS_FAST);
+        rc = wgb_self_attention_ex(M->att, M->qr, kb, vb, M->dt, T, m.nh, m.nkvh, m.dh, m.dh, total_len, scale,
+                                   M->attn_ws, M->attn_ws_bytes, s);
+        wgb_set_numerics(prev);
+        if (rc) return rc;
+    } else {
+        if ((rc = attn_decode(M->dt, M->att, M->qr, M->layer_k(l), M->layer_v(l), M->seq_stride, M->lens, T,
+                              (int)m.nh, (int)m.nkvh, (int)m.dh, (int)m.maxseq, scale, M->attn_ws, ref, s)))
+            return rc;
+    }
+    // o_proj with the residual add fused: x = x + o(att)
+    if ((rc = linear_forward(M->dt, M->x, M->att, w.o_w, nullptr, M->x, T, hs, (int)(m.nh * m.dh), ref, s))) return rc;
+    if ((rc = wgb_rms_norm(M->xn, M->x, w.mlp_norm, M->dt, T, hs, m.epsilon, s))) return rc;
+    if ((rc = linear_forward(M->dt, M->gu, M->xn, w.gu_w, nullptr, nullptr, T, 2 * di, hs, ref, s))) return rc;
+    {
+        const size_t n = (size_t)T * di;
+        const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)sm_count() * 8);
+        WGB_DISPATCH_FLOAT(M->dt, Tt,
+            if (ref) swiglu_rows_kernel<Tt, true><<<blocks, 256, 0, s>>>((Tt *)M->act, (const Tt *)M->gu, T, di);
+            else swiglu_rows_kernel<Tt, false><<<blocks, 256, 0, s>>>((Tt *)M->act, (const Tt *)M->gu, T, di));
+        if ((rc = cuda_err("swiglu_rows"))) return rc;
+    }
+    return linear_forward(M->dt, M->x, M->act, w.down_w, nullptr, M->x, T, hs, di, ref, s);
+}
+
+// Decode step body for sequences [0, B) (captured into a graph).
+int decode_body(wgbQwen2Model *M, int B, bool ref) {
+    const wgbQwen2Meta &m = M->m;
+    cudaStream_t s = M->stream;
+    int rc;
+    decode_begin_kernel<<<(B + 127) / 128, 128, 0, s>>>(M->pos, M->lens, B);
+    if ((rc = wgb_embedding(M->x, M->tokens, M->in_embed, M->dt, B, m.hs, m.voc, s))) return rc;
+    for (size_t l = 0; l < m.nlayer; l++)
+        if ((rc = run_layer(M, l, B, -1, 0, ref))) return rc;
+    if ((rc = wgb_rms_norm(M->xn, M->x, M->out_norm, M->dt, B, m.hs, m.epsilon, s))) return rc;
+    if ((rc = linear_forward(M->dt, M->logits, M->xn, M->out_embed, nullptr, nullptr, B, (int)m.voc, (int)m.hs, ref, s)))
+        return rc;
+    if ((rc = wgb_argmax_rows(M->tokens, nullptr, M->logits, M->dt, B, m.voc, s))) return rc;
+    decode_end_kernel<<<(B + 127) / 128, 128, 0, s>>>(M->lens, B, (int)m.maxseq);
+    return cuda_err("decode_end");
+}
+
+int prefill_impl(wgbQwen2Model *M, int seq, const int64_t *ids_host, size_t n, bool ref) {
+    const wgbQwen2Meta &m = M->m;
+    cudaStream_t s = M->stream;
+    size_t cache_len = M->h_lens[seq];
+    WGB_REQUIRE(cache_len + n <= m.maxseq, WGB_ERR_OUT_OF_RANGE, "prefill: %zu + %zu tokens exceed maxseq %zu", cache_len,
+                n, (size_t)m.maxseq);
+    int rc;
+    for (size_t off = 0; off < n; off += M->chunk) {
+        const int T = (int)std::min<size_t>(M->chunk, n - off);
+        if (M->h_pinned_n < (size_t)T) return set_error(WGB_ERR_INVALID_ARGUMENT, "staging too small");
+        // stage ids through pinned memory; the copy must finish before the buffer is reused
+        if (cudaStreamSynchronize(s) != cudaSuccess) return cuda_err("prefill sync");
+        memcpy(M->h_pinned, ids_host + off, (size_t)T * sizeof(int64_t));
+        int64_t *ids_dev = M->pos + M->chunk;  // second half of the position buffer holds ids
+        if (cudaMemcpyAsync(ids_dev, M->h_pinned, (size_t)T * sizeof(int64_t), cudaMemcpyHostToDevice, s) != cudaSuccess)
+            return cuda_err("prefill H2D");
+        fill_positions_kernel<<<(T + 255) / 256, 256, 0, s>>>(M->pos, (int64_t)cache_len, T);
+        if ((rc = wgb_embedding(M->x, ids_dev, M->in_embed, M->dt, T, m.hs, m.voc, s))) return rc;
+        const size_t total = cache_len + T;
+        for (size_t l = 0; l < m.nlayer; l++)
+            if ((rc = run_layer(M, l, T, seq, total, ref))) return rc;
+        cache_len = total;
+        if (off + T == n) {
+            const char *last = (const char *)M->x + (size_t)(T - 1) * m.hs * M->es;
+            void *lg = (char *)M->logits + (size_t)seq * m.voc * M->es;
+            if ((rc = wgb_rms_norm(M->xn, last, M->out_norm, M->dt, 1, m.hs, m.epsilon, s))) return rc;
+            if ((rc = linear_forward(M->dt, lg, M->xn, M->out_embed, nullptr, nullptr, 1, (int)m.voc, (int)m.hs, ref, s)))
+                return rc;
+            if ((rc = wgb_argmax_rows(M->tokens + seq, nullptr, lg, M->dt, 1, m.voc, s))) return rc;
+        }
+    }
+    M->h_lens[seq] = cache_len;
+    int64_t l64 = (int64_t)cache_len;
+    if (cudaMemcpyAsync(M->lens + seq, &l64, sizeof(int64_t), cudaMemcpyHostToDevice, s) != cudaSuccess)
+        return cuda_err("prefill lens");
+    if (cudaStreamSynchronize(s) != cudaSuccess) return cuda_err("prefill");
+    return WGB_OK;
+}
+
+int get_graph(wgbQwen2Model *M, int B, bool ref, cudaGraphExec_t *out) {
+    auto &g = M->graphs[ref ? 1 : 0];
+    if (g.size() < (size_t)M->max_batch + 1) g.resize(M->max_batch + 1, nullptr);
+    if (g[B]) {
+        *out = g[B];
+        return WGB_OK;
+    }
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(M->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        return cuda_err("begin capture");
+    int rc = decode_body(M, B, ref);
+    cudaError_t e = cudaStreamEndCapture(M->stream, &graph);
+    if (rc) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_err("end capture");
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return cuda_err("graph instantiate");
+    g[B] = exec;
+    *out = exec;
+    return WGB_OK;
+}
+
+// Host table with the reference's exact expressions (rope_cpu.cpp:13-36).
+std::vector<float2> build_rope_table(size_t maxseq, size_t dh, float theta) {
+    const size_t half = dh / 2;
+    std::vector<float> denom(half);
+    for (size_t j = 0; j < half; ++j) denom[j] = ::powf(theta, (2.0f * (float)j) / (float)dh);
+    std::vector<float2> t(maxseq * half);
+    for (size_t p = 0; p < maxseq; ++p) {
+        const float pf = (float)(int64_t)p;
+        for (size_t j = 0; j < half; ++j) {
+            const float phi = pf / denom[j];
+            t[p * half + j] = make_float2(::cosf(phi), ::sinf(phi));
+        }
+    }
+    return t;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wgb_qwen2_create(const wgbQwen2Meta *meta, int device, int max_batch, wgbQwen2Model **out) {
+    WGB_REQUIRE(meta && out, WGB_ERR_INVALID_ARGUMENT, "wgb_qwen2_create: null argument");
+    WGB_REQUIRE(meta->dtype == WGINFER_DTYPE_BF16 || meta->dtype == WGINFER_DTYPE_F32 || meta->dtype == WGINFER_DTYPE_F16,
+                WGB_ERR_UNSUPPORTED_DTYPE, "wgb_qwen2_create: dtype %d", meta->dtype);
+    WGB_REQUIRE(meta->nlayer > 0 && meta->hs > 0 && meta->nh > 0 && meta->nkvh > 0 && meta->nh % meta->nkvh == 0 &&
+                    meta->dh > 0 && meta->dh % 2 == 0 && meta->di > 0 && meta->maxseq > 0 && meta->voc > 0,
+                WGB_ERR_INVALID_ARGUMENT, "wgb_qwen2_create: bad meta");
+    WGB_REQUIRE(max_batch >= 1 && max_batch <= 4096, WGB_ERR_INVALID_ARGUMENT, "wgb_qwen2_create: max_batch %d", max_batch);
+    if (cudaSetDevice(device) != cudaSuccess) return cuda_err("wgb_qwen2_create: cudaSetDevice");
+    auto *M = new wgbQwen2Model();
+    M->m = *meta;
+    M->device = device;
+    M->max_batch = max_batch;
+    M->dt = (wginferDataType_t)meta->dtype;
+    M->es = dsize(meta->dtype);
+    M->chunk = (int)std::min<size_t>(meta->maxseq, 2048);
+    const wgbQwen2Meta &m = M->m;
+    const size_t es = M->es, rows = std::max<size_t>(max_batch, M->chunk);
+    M->seq_stride = m.maxseq * m.nkvh * m.dh;
+    const bool ref_ws = true;  // size the workspace for either numerics mode
+    const size_t ws_dec = std::max(attn_decode_workspace(max_batch, (int)m.nh, (int)m.nkvh, (int)m.dh, (int)m.maxseq, false),
+                                   attn_decode_workspace(max_batch, (int)m.nh, (int)m.nkvh, (int)m.dh, (int)m.maxseq, ref_ws));
+    int prev = wgb_get_numerics();
+    wgb_set_numerics(WGB_NUMERICS_FAST);
+    size_t ws_pre = wgb_self_attention_workspace_size(M->chunk, m.nh, m.nkvh, m.dh, m.dh, m.maxseq);
+    wgb_set_numerics(WGB_NUMERICS_REFERENCE);
+    ws_pre = std::max(ws_pre, wgb_self_attention_workspace_size(M->chunk, m.nh, m.nkvh, m.dh, m.dh, m.maxseq));
+    wgb_set_numerics(prev);
+    M->attn_ws_bytes = std::max<size_t>(std::max(ws_dec, ws_pre), 256);
+
+    // arena plan
+    struct Item { void **p; size_t bytes; };
+    std::vector<Item> items;
+    M->L.resize(m.nlayer);
+    items.push_back({&M->in_embed, m.voc * m.hs * es});
+    items.push_back({&M->out_embed, m.voc * m.hs * es});
+    items.push_back({&M->out_norm, m.hs * es});
+    for (size_t l = 0; l < m.nlayer; l++) {
+        LayerW &w = M->L[l];
+        items.push_back({&w.attn_norm, m.hs * es});
+        items.push_back({&w.qkv_w, M->nq() * m.hs * es});
+        items.push_back({&w.qkv_b, M->nq() * es});
+        items.push_back({&w.o_w, m.hs * m.nh * m.dh * es});
+        items.push_back({&w.mlp_norm, m.hs * es});
+        items.push_back({&w.gu_w, 2 * m.di * m.hs * es});
+        items.push_back({&w.down_w, m.hs * m.di * es});
+    }
+    items.push_back({(void **)&M->rope_table, m.maxseq * (m.dh / 2) * sizeof(float2)});
+    items.push_back({&M->kc, m.nlayer * (size_t)max_batch * M->seq_stride * es});
+    items.push_back({&M->vc, m.nlayer * (size_t)max_batch * M->seq_stride * es});
+    items.push_back({(void **)&M->lens, (size_t)max_batch * 8});
+    items.push_back({(void **)&M->tokens, (size_t)max_batch * 8});
+    items.push_back({(void **)&M->pos, 2 * rows * 8});
+    items.push_back({&M->x, rows * m.hs * es});
+    items.push_back({&M->xn, rows * m.hs * es});
+    items.push_back({&M->qkv, rows * M->nq() * es});
+    items.push_back({&M->qr, rows * m.nh * m.dh * es});
+    items.push_back({&M->att, rows * m.nh * m.dh * es});
+    items.push_back({&M->gu, rows * 2 * m.di * es});
+    items.push_back({&M->act, rows * m.di * es});
+    items.push_back({&M->logits, (size_t)max_batch * m.voc * es});
+    items.push_back({&M->attn_ws, M->attn_ws_bytes});
+    size_t total = 0;
+    for (auto &it : items) total += align256(it.bytes);
+    if (cudaMalloc((void **)&M->arena, total) != cudaSuccess) {
+        cudaGetLastError();
+        delete M;
+        return set_error(WGB_ERR_NO_MEMORY, "wgb_qwen2_create: arena of %zu bytes", total);
+    }
+    M->arena_bytes = total;
+    size_t off = 0;
+    for (auto &it : items) {
+        *it.p = M->arena + off;
+        off += align256(it.bytes);
+    }
+    int rc = WGB_OK;
+    if (cudaStreamCreateWithFlags(&M->stream, cudaStreamNonBlocking) != cudaSuccess) rc = cuda_err("stream");
+    // zero everything (biases default to zero, like the reference's dummy biases)
+    if (!rc && cudaMemsetAsync(M->arena, 0, total, M->stream) != cudaSuccess) rc = cuda_err("arena memset");
+    auto table = build_rope_table(m.maxseq, m.dh, m.theta);
+    if (!rc && cudaMemcpyAsync(M->rope_table, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice,
+                               M->stream) != cudaSuccess)
+        rc = cuda_err("rope table");
+    M->h_pinned_n = (size_t)M->chunk;
+    if (!rc && cudaMallocHost((void **)&M->h_pinned, M->h_pinned_n * sizeof(int64_t)) != cudaSuccess)
+        rc = cuda_err("pinned staging");
+    if (!rc && cudaStreamSynchronize(M->stream) != cudaSuccess) rc = cuda_err("create sync");
+    attn_prepare();
+    dev_error_ptr();  // resolve the error-word address outside any graph capture
+    M->h_lens.assign(max_batch, 0);
+    if (rc) {
+        wgb_qwen2_destroy(M);
+        return rc;
+    }
+    *out = M;
+    return WGB_OK;
+}
+
+int wgb_qwen2_destroy(wgbQwen2Model *M) {
+    if (!M) return WGB_OK;
+    cudaSetDevice(M->device);
+    if (M->stream) cudaStreamSynchronize(M->stream);
+    for (auto &g : M->graphs)
+        for (auto e : g)
+            if (e) cudaGraphExecDestroy(e);
+    if (M->h_pinned) cudaFreeHost(M->h_pinned);
+    if (M->arena) cudaFree(M->arena);
+    if (M->stream) cudaStreamDestroy(M->stream);
+    delete M;
+    return WGB_OK;
+}
+
+int wgb_qwen2_set_weight(wgbQwen2Model *M, const char *name, int layer, const void *src, size_t bytes, int on_host) {
+    WGB_REQUIRE(M && name && src, WGB_ERR_INVALID_ARGUMENT, "wgb_qwen2_set_weight: null argument");
+    const wgbQwen2Meta &m = M->m;
+    const size_t es = M->es;
+    std::string n(name);
+    void *dst = nullptr;
+    size_t want = 0;
+    if (layer < 0) {
+        if (n == "in_embed") dst = M->in_embed, want = m.voc * m.hs * es;
+        else if (n == "out_embed") dst = M->out_embed, want = m.voc * m.hs * es;
+        else if (n == "out_norm_w") dst = M->out_norm, want = m.hs * es;
+    } else {
+        WGB_REQUIRE((size_t)layer < m.nlayer, WGB_ERR_OUT_OF_RANGE, "layer %d out of range", layer);
+        LayerW &w = M->L[layer];
+        const size_t qn = m.nh * m.dh, kn = m.nkvh * m.dh;
+        if (n == "attn_norm_w") dst = w.attn_norm, want = m.hs * es;
+        else if (n == "attn_q_w") dst = w.qkv_w, want = qn * m.hs * es;
+        else if (n == "attn_k_w") dst = (char *)w.qkv_w + qn * m.hs * es, want = kn * m.hs * es;
+        else if (n == "attn_v_w") dst = (char *)w.qkv_w + (qn + kn) * m.hs * es, want = kn * m.hs * es;
+        else if (n == "attn_q_b") dst = w.qkv_b, want = qn * es;
+        else if (n == "attn_k_b") dst = (char *)w.qkv_b + qn * es, want = kn * es;
+        else if (n == "attn_v_b") dst = (char *)w.qkv_b + (qn + kn) * es, want = kn * es;
+        else if (n == "attn_o_w") dst = w.o_w, want = m.hs * qn * es;
+        else if (n == "mlp_norm_w") dst = w.mlp_norm, want = m.hs * es;
+        else if (n == "mlp_gate_w") dst = w.gu_w, want = m.di * m.hs * es;
+        else if (n == "mlp_up_w") dst = (char *)w.gu_w + m.di * m.hs * es, want = m.di * m.hs * es;
+        else if (n == "mlp_down_w") dst = w.down_w, want = m.hs * m.di * es;
+    }
+    WGB_REQUIRE(dst != nullptr, WGB_ERR_INVALID_ARGUMENT, "unknown Qwen2 weight: %s", name);
+    WGB_REQUIRE(bytes == want, WGB_ERR_INVALID_ARGUMENT, "weight %s: %zu bytes given, %zu expected", name, bytes, want);
+    cudaSetDevice(M->device);
+    if (cudaMemcpyAsync(dst, src, bytes, on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, M->stream) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(M->stream) != cudaSuccess)
+        return cuda_err("wgb_qwen2_set_weight");
+    return WGB_OK;
+}
+
+int wgb_qwen2_reset_cache(wgbQwen2Model *M) {
+    WGB_REQUIRE(M, WGB_ERR_INVALID_ARGUMENT, "null model");
+    cudaSetDevice(M->device);
+    std::fill(M->h_lens.begin(), M->h_lens.end(), 0);
+    if (cudaMemsetAsync(M->lens, 0, (size_t)M->max_batch * 8, M->stream) != cudaSuccess ||
+        cudaStreamSynchronize(M->stream) != cudaSuccess)
+        return cuda_err("reset_cache");
+    return WGB_OK;
+}
+
+int wgb_qwen2_prefill(wgbQwen2Model *M, int seq, const int64_t *ids, size_t n) {
+    WGB_REQUIRE(M && ids && n > 0, WGB_ERR_INVALID_ARGUMENT, "wgb_qwen2_prefill: bad argument");
+    WGB_REQUIRE(seq >= 0 && seq < M->max_batch, WGB_ERR_OUT_OF_RANGE, "sequence %d", seq);
+    cudaSetDevice(M->device);
+    return prefill_impl(M, seq, ids, n, wgb_get_numerics() == WGB_NUMERICS_REFERENCE);
+}
+
+int wgb_qwen2_decode_step(wgbQwen2Model *M, int B) {
+    WGB_REQUIRE(M && B >= 1 && B <= M->max_batch, WGB_ERR_INVALID_ARGUMENT, "wgb_qwen2_decode_step: batch %d", B);
+    cudaSetDevice(M->device);
+    for (int b = 0; b < B; b++)
+        WGB_REQUIRE(M->h_lens[b] < M->m.maxseq, WGB_ERR_OUT_OF_RANGE, "sequence %d is full (%zu)", b,
+                    (size_t)M->m.maxseq);
+    cudaGraphExec_t g;
+    int rc = get_graph(M, B, wgb_get_numerics() == WGB_NUMERICS_REFERENCE, &g);
+    if (rc) return rc;
+    if (cudaGraphLaunch(g, M->stream) != cudaSuccess) return cuda_err("graph launch");
+    for (int b = 0; b < B; b++) M->h_lens[b]++;
+    return WGB_OK;
+}
+
+int wgb_qwen2_infer(wgbQwen2Model *M, const int64_t *ids, size_t n, int top_k, float top_p, float temperature,
+                    int64_t *next) {
+    WGB_REQUIRE(M && ids && n > 0 && next, WGB_ERR_INVALID_ARGUMENT, "wgb_qwen2_infer: bad argument");
+    cudaSetDevice(M->device);
+    const bool ref = wgb_get_numerics() == WGB_NUMERICS_REFERENCE;
+    int rc;
+    if (n == 1) {
+        WGB_REQUIRE(M->h_lens[0] < M->m.maxseq, WGB_ERR_OUT_OF_RANGE, "sequence 0 is full");
+        M->h_pinned[0] = ids[0];
+        if (cudaMemcpyAsync(M->tokens, M->h_pinned, sizeof(int64_t), cudaMemcpyHostToDevice, M->stream) != cudaSuccess)
+            return cuda_err("infer H2D");
+        if ((rc = wgb_qwen2_decode_step(M, 1))) return rc;
+    } else {
+        if ((rc = prefill_impl(M, 0, ids, n, ref))) return rc;
+    }
+    const bool greedy = top_k == 1 && top_p >= 1.0f && std::fabs(temperature - 1.0f) < 1e-6f;
+    if (greedy) {
+        if (cudaMemcpyAsync(M->h_pinned, M->tokens, sizeof(int64_t), cudaMemcpyDeviceToHost, M->stream) != cudaSuccess ||
+            cudaStreamSynchronize(M->stream) != cudaSuccess)
+            return cuda_err("infer D2H");
+        *next = M->h_pinned[0];
+        return WGB_OK;
+    }
+    const size_t V = M->m.voc;
+    std::vector<uint16_t> h16;
+    std::vector<float> lg(V);
+    if (M->dt == WGINFER_DTYPE_F32) {
+        if (cudaMemcpyAsync(lg.data(), M->logits, V * 4, cudaMemcpyDeviceToHost, M->stream) != cudaSuccess)
+            return cuda_err("logits D2H");
+    } else {
+        h16.resize(V);
+        if (cudaMemcpyAsync(h16.data(), M->logits, V * 2, cudaMemcpyDeviceToHost, M->stream) != cudaSuccess)
+            return cuda_err("logits D2H");
+    }
+    if (cudaStreamSynchronize(M->stream) != cudaSuccess) return cuda_err("logits sync");
+    if (M->dt == WGINFER_DTYPE_BF16) {
+        for (size_t i = 0; i < V; i++) {
+            uint32_t u = (uint32_t)h16[i] << 16;
+            memcpy(&lg[i], &u, 4);
+        }
+    } else if (M->dt == WGINFER_DTYPE_F16) {
+        for (size_t i = 0; i < V; i++) {
+            __half_raw r;
+            r.x = h16[i];
+            lg[i] = __half2float(__half(r));
+        }
+    }
+    *next = sample_host(lg, top_k, top_p, temperature);
+    return WGB_OK;
+}
+
+int64_t *wgb_qwen2_token_buffer(wgbQwen2Model *M) { return M ? M->tokens : nullptr; }
+wginferStream_t wgb_qwen2_stream(wgbQwen2Model *M) { return M ? (wginferStream_t)M->stream : nullptr; }
+size_t wgb_qwen2_cache_len(wgbQwen2Model *M, int seq) {
+    return (M && seq >= 0 && seq < M->max_batch) ? M->h_lens[seq] : 0;
+}
+const void *wgb_qwen2_logits(wgbQwen2Model *M, int seq) {
+    return (M && seq >= 0 && seq < M->max_batch) ? (const char *)M->logits + (size_t)seq * M->m.voc * M->es : nullptr;
+}
+
+int wgb_qwen2_read_tokens(wgbQwen2Model *M, int64_t *host, int batch) {
+    WGB_REQUIRE(M && host && batch >= 1 && batch <= M->max_batch, WGB_ERR_INVALID_ARGUMENT, "read_tokens");
+    cudaSetDevice(M->device);
+    if (cudaMemcpyAsync(host, M->tokens, (size_t)batch * 8, cudaMemcpyDeviceToHost, M->stream) != cudaSuccess ||
+        cudaStreamSynchronize(M->stream) != cudaSuccess)
+        return cuda_err("read_tokens");
+    return WGB_OK;
+}
+
+int wgb_qwen2_read_logits(wgbQwen2Model *M, int seq, float *host) {
+    WGB_REQUIRE(M && host && seq >= 0 && seq < M->max_batch, WGB_ERR_INVALID_ARGUMENT, "read_logits");
+    cudaSetDevice(M->device);
+    const size_t V = M->m.voc;
+    const char *src = (const char *)M->logits + (size_t)seq * V * M->es;
+    if (M->dt == WGINFER_DTYPE_F32) {
+        if (cudaMemcpyAsync(host, src, V * 4, cudaMemcpyDeviceToHost, M->stream) != cudaSuccess ||
+            cudaStreamSynchronize(M->stream) != cudaSuccess)
+            return cuda_err("read_logits");
+        return WGB_OK;
+    }
+    std::vector<uint16_t> h(V);
+    if (cudaMemcpyAsync(h.data(), src, V * 2, cudaMemcpyDeviceToHost, M->stream) != cudaSuccess ||
+        cudaStreamSynchronize(M->stream) != cudaSuccess)
+        return cuda_err("read_logits");
+    for (size_t i = 0; i < V; i++) {
+        if (M->dt == WGINFER_DTYPE_BF16) {
+            uint32_t u = (uint32_t)h[i] << 16;
+            memcpy(&host[i], &u, 4);
+        } else {
+            __half_raw r;
+            r.x = h[i];
+            host[i] = __half2float(__half(r));
+        }
+    }
+    return WGB_OK;
+}
+
+}  // extern "C"
