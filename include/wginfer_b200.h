@@ -135,6 +135,26 @@ __export int wgb_self_attention_ex(void *attn_val, const void *q, const void *k,
                                    float scale, void *workspace, size_t workspace_bytes,
                                    wginferStream_t stream);
 
+/* wgb_self_attention for callers that cannot allocate device memory: code
+ * running inside an allocator or memory-pool callback (allocating there would
+ * re-enter the allocator), host runtimes that own all device memory and give
+ * their kernels no allocation hook, and threads that must not block in the
+ * driver. No counterpart in the reference. Its scratch is one file-scope
+ * device array of wgb_self_attention_noalloc_max_scratch() bytes (4 MiB),
+ * held by every GPU that loads the library until exit; sizes whose scratch
+ * would exceed it return WGB_ERR_OUT_OF_RANGE. The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress), so make that
+ * first call before any stream capture. Calls allocate nothing. All calls on
+ * a device share the array, which keeps the last call's contents; nothing in
+ * it has to start at zero (every scratch word a call reads is written earlier
+ * in that call), but calls whose kernels overlap on the same device, e.g. on
+ * two streams, race: serialise them, e.g. on one stream. */
+__export int wgb_self_attention_noalloc(void *attn_val, const void *q, const void *k, const void *v,
+                                        wginferDataType_t dtype, size_t seqlen, size_t nhead,
+                                        size_t nkvhead, size_t d, size_t dv, size_t total_len,
+                                        float scale, wginferStream_t stream);
+__export size_t wgb_self_attention_noalloc_max_scratch(void);
+
 /* out = up * gate / (1 + exp(-gate)). Replaces ops::nvidia::swiglu
  * (src/ops/swiglu/nvidia/swiglu_nvidia.cuh:6-7). */
 __export int wgb_swiglu(void *out, const void *gate, const void *up, wginferDataType_t dtype,

@@ -38,6 +38,8 @@ SIGNATURES = {
     "wgb_self_attention": (_I, [_P, _P, _P, _P, _I, _S, _S, _S, _S, _S, _S, _F, _P]),
     "wgb_self_attention_workspace_size": (_S, [_S, _S, _S, _S, _S, _S]),
     "wgb_self_attention_ex": (_I, [_P, _P, _P, _P, _I, _S, _S, _S, _S, _S, _S, _F, _P, _S, _P]),
+    "wgb_self_attention_noalloc": (_I, [_P, _P, _P, _P, _I, _S, _S, _S, _S, _S, _S, _F, _P]),
+    "wgb_self_attention_noalloc_max_scratch": (_S, []),
     "wgb_swiglu": (_I, [_P, _P, _P, _I, _S, _P]),
     "wgb_qwen2_create": (_I, [_P, _I, _I, _P]),
     "wgb_qwen2_destroy": (_I, [_P]),

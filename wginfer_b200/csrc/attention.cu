@@ -469,3 +469,69 @@ extern "C" int wgb_self_attention(void *attn_val, const void *q, const void *k, 
     return wgb_self_attention_ex(attn_val, q, k, v, dtype, seqlen, nhead, nkvhead, d, dv, total_len, scale, ws, need,
                                  stream);
 }
+
+// ---- allocation-free variant -------------------------------------------------
+// Some callers cannot call cudaMalloc: code running inside an allocator or
+// memory-pool callback (re-entering the allocator would deadlock), host
+// runtimes that own every byte of device memory and give their kernels no
+// allocation hook, and real-time threads that must not block in the driver.
+// wgb_self_attention_noalloc serves them with a fixed scratch array compiled
+// into this library instead of the lazily allocated workspace.
+#include <mutex>
+
+namespace wgb {
+namespace {
+
+constexpr size_t kStaticScratchBytes = 4u << 20;  // 4 MiB, held by every GPU that loads the library
+static __device__ __align__(256) unsigned char g_attn_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mu;
+void *g_static_ptr[64];  // device address of the array, per device; set once
+
+// The array's name in host code is only a host-side stand-in; the device
+// address must be looked up with the device current.
+int static_scratch(void **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "wgb_self_attention_noalloc: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return set_error(WGB_ERR_INVALID_ARGUMENT, "device id %d", dev);
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (g_static_ptr[dev] == nullptr) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return set_error(WGB_ERR_CUDA, "wgb_self_attention_noalloc: cudaGetSymbolAddress: %s",
+                             cudaGetErrorString(e));
+        g_static_ptr[dev] = p;
+    }
+    *out = g_static_ptr[dev];
+    return WGB_OK;
+}
+
+}  // namespace
+}  // namespace wgb
+
+extern "C" size_t wgb_self_attention_noalloc_max_scratch(void) { return wgb::kStaticScratchBytes; }
+
+extern "C" int wgb_self_attention_noalloc(void *attn_val, const void *q, const void *k, const void *v,
+                                          wginferDataType_t dtype, size_t seqlen, size_t nhead, size_t nkvhead,
+                                          size_t d, size_t dv, size_t total_len, float scale,
+                                          wginferStream_t stream) {
+    if (seqlen == 0 || nhead == 0) return WGB_OK;
+    int rc = wgb::check_args(attn_val, q, k, v, seqlen, nhead, nkvhead, d, dv, total_len);
+    if (rc) return rc;
+    const size_t need = wgb_self_attention_workspace_size(seqlen, nhead, nkvhead, d, dv, total_len);
+    WGB_REQUIRE(need <= wgb::kStaticScratchBytes, WGB_ERR_OUT_OF_RANGE,
+                "wgb_self_attention_noalloc: these sizes need %zu bytes of scratch; the static array holds %zu",
+                need, wgb::kStaticScratchBytes);
+    void *ws = nullptr;
+    if (need) {
+        rc = wgb::static_scratch(&ws);
+        if (rc) return rc;
+    }
+    // Every scratch word the kernels read is written earlier in the same call
+    // (each key slice stores its max, sum and partial output before the
+    // combine reads them), so nothing needs clearing between calls.
+    return wgb_self_attention_ex(attn_val, q, k, v, dtype, seqlen, nhead, nkvhead, d, dv, total_len, scale, ws,
+                                 need, stream);
+}
