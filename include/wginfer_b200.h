@@ -218,6 +218,14 @@ __export wginferStream_t wgb_qwen2_stream(wgbQwen2Model *model);
 __export size_t wgb_qwen2_cache_len(wgbQwen2Model *model, int seq);
 /* Device pointer to the last logits row of sequence `seq` (dtype, voc). */
 __export const void *wgb_qwen2_logits(wgbQwen2Model *model, int seq);
+/* One decode step (like wgb_qwen2_decode_step) launched eagerly with a CUDA
+ * event after every launch, for a per-launch device-time breakdown: us[i]
+ * is the time of launch i (microseconds) and names holds one launch name per
+ * line. Events between launches serialise them, so the sum exceeds a graph
+ * step; the shares are what it is for. */
+__export int wgb_qwen2_trace_step(wgbQwen2Model *model, int batch, int max_launches, float *us, char *names,
+                                  size_t names_cap, int *n_launches);
+
 /* Synchronous host copies of the token buffer (int64[batch]) and of the
  * last logits row of `seq` widened to f32 (voc floats). */
 __export int wgb_qwen2_read_tokens(wgbQwen2Model *model, int64_t *host, int batch);

@@ -77,7 +77,12 @@ def test_bad_shapes_rejected_before_device_work():
     assert l.wgb_rope(p, p, p, 15, 1, 1, 4, C.c_float(-1.0), None) == 1          # theta <= 0
     assert l.wgb_self_attention(p, p, p, p, 15, 1, 3, 2, 4, 4, 1, C.c_float(1.0), None) == 1  # nh % nkvh
     assert l.wgb_add(p, p, p, 6, 4, None) == 2                                    # int64 is not a float dtype
-    assert l.wgb_self_attention_ex(p, p, p, p, 15, 1, 12, 2, 128, 128, 4096, C.c_float(1.0), None, 0, None) == 1
+    _lib.set_numerics(_lib.NUMERICS_REFERENCE)  # long caches need score scratch there; none given
+    try:
+        assert l.wgb_self_attention_ex(p, p, p, p, 15, 1, 12, 2, 128, 128, 12000, C.c_float(1.0), None, 0, None) == 1
+    finally:
+        _lib.set_numerics(_lib.NUMERICS_FAST)
+    assert l.wgb_self_attention(p, p, p, p, 15, 1, 12, 2, 512, 512, 8, C.c_float(1.0), None) == 1  # dims too large
 
 
 def test_zero_sizes_are_noops():

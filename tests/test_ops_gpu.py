@@ -175,24 +175,47 @@ def test_linear_unaligned_and_ragged(oracle, cuda, mode):
 
 
 def test_attention_workspace_contract(cuda):
+    """FAST needs no workspace (the cluster folds its key slices in shared
+    memory); REFERENCE keeps one score per key in the workspace once the cache
+    is longer than shared memory holds."""
     import ctypes as C
     from wginfer_b200 import _lib
     l = _lib.lib()
-    need = l.wgb_self_attention_workspace_size(1, 12, 2, 128, 128, 4096)
-    assert need > 0
+    assert l.wgb_self_attention_workspace_size(1, 12, 2, 128, 128, 4096) == 0
+    L = 12000
     q = _bf16((1, 12, 128), 1)
-    k = _bf16((4096, 2, 128), 2)
-    v = _bf16((4096, 2, 128), 3)
+    k = _bf16((L, 2, 128), 2)
+    v = _bf16((L, 2, 128), 3)
     out = torch.empty_like(q)
     p = lambda t: C.c_void_p(t.data_ptr())
     st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-    rc = l.wgb_self_attention_ex(p(out), p(q), p(k), p(v), 15, 1, 12, 2, 128, 128, 4096, C.c_float(0.088), None, 0, st)
-    assert rc == 1
-    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
-    rc = l.wgb_self_attention_ex(p(out), p(q), p(k), p(v), 15, 1, 12, 2, 128, 128, 4096, C.c_float(0.088), p(ws),
-                                 need, st)
-    assert rc == 0
-    out2 = torch.empty_like(q)
-    ops.self_attention(out2, q, k, v, 0.088)
+    with numerics("reference"):
+        need = l.wgb_self_attention_workspace_size(1, 12, 2, 128, 128, L)
+        assert need == 12 * L * 4
+        rc = l.wgb_self_attention_ex(p(out), p(q), p(k), p(v), 15, 1, 12, 2, 128, 128, L, C.c_float(0.088), None, 0, st)
+        assert rc == 1
+        ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+        rc = l.wgb_self_attention_ex(p(out), p(q), p(k), p(v), 15, 1, 12, 2, 128, 128, L, C.c_float(0.088), p(ws),
+                                     need, st)
+        assert rc == 0
+        out2 = torch.empty_like(q)
+        ops.self_attention(out2, q, k, v, 0.088)
     torch.cuda.synchronize()
     assert torch.equal(out, out2)
+
+
+@pytest.mark.parametrize("mode", ["fast", "reference"])
+@pytest.mark.parametrize("L", [1, 63, 64, 65, 700, 2304])
+def test_attention_decode_lengths(oracle, cuda, mode, L):
+    """Single-query decode over cache lengths around the tile size."""
+    q, k, v = _bf16((1, 12, 128), L), _bf16((L, 2, 128), L + 1), _bf16((L, 2, 128), L + 2)
+    out = torch.empty_like(q)
+    with numerics(mode):
+        ops.self_attention(out, q, k, v, 1 / 128 ** 0.5)
+    h = lambda t: t.cpu().view(torch.int16).numpy().view(np.uint16)
+    want = np.zeros((1, 12, 128), np.uint16)
+    oracle.self_attention(want, h(q), h(k), h(v), 1 / 128 ** 0.5, 15)
+    if mode == "reference":
+        assert np.array_equal(h(out), want)
+    else:
+        np.testing.assert_allclose(as_f32(h(out)), as_f32(want), rtol=2e-2, atol=1e-2)

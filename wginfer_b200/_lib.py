@@ -53,6 +53,7 @@ SIGNATURES = {
     "wgb_qwen2_cache_len": (_S, [_P, _I]),
     "wgb_qwen2_logits": (_P, [_P, _I]),
     "wgb_qwen2_read_tokens": (_I, [_P, _P, _I]),
+    "wgb_qwen2_trace_step": (_I, [_P, _I, _I, _P, _P, _S, _P]),
     "wgb_qwen2_read_logits": (_I, [_P, _I, _P]),
 }
 

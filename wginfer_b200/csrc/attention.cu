@@ -1,32 +1,43 @@
 // self_attention: causal GQA attention over a KV cache.
 //
-// FAST (flash-decode, split-K): a CTA owns one query row, a block of HPC
-// heads that share one kv head, and one slice of the visible keys. K/V tiles
-// of kKT keys are staged in shared memory once for all HPC heads (GQA
-// reuse), scores use an online softmax in f32, and each slice writes
-// (max, sum, unnormalised output) to a workspace that a combine kernel folds
-// with a log-sum-exp rescale. Slices are chosen so that short queries (decode)
-// still fill the SMs. Roofline at decode: HBM, (S*nh*d + 2*L*nkvh*d +
-// S*nh*dv) * size bytes.
+// FAST (flash-decode, split-K over a thread-block cluster): a cluster of up
+// to 8 CTAs owns one query row and a block of HPC heads that share one kv
+// head; each CTA takes one slice of the visible keys. K/V tiles of kKT keys
+// stream into shared memory with cp.async (double-buffered) and are used once
+// for all HPC heads (GQA reuse); scores use an online softmax in f32. The
+// slices then meet in distributed shared memory: CTA 0 of the cluster reads
+// the others' (max, sum, unnormalised output) and writes the normalised row,
+// so there is no workspace and no second launch. The slice count adapts to
+// each row's visible length, so a decode graph captured once stays balanced
+// as the caches grow. Roofline at decode: HBM,
+// (S*nh*d + 2*L*nkvh*d + S*nh*dv) * size bytes.
 //
 // REFERENCE: one CTA per (query, head) reproduces
 // src/ops/self_attention/cpu/self_attention_cpu.cpp:35-89 step for step:
 // sequential dot products, -1e9 for masked keys, max, exp, a sequential sum
 // over every key, division, and a sequential sum over keys of the rounded
-// products p * v.
+// products p * v. K and V stream through shared memory in chunks so that the
+// serial chains read at shared-memory latency.
+#include <cooperative_groups.h>
+#include <cuda_pipeline.h>
 #include <float.h>
 
 #include "common.cuh"
 
+namespace cg = cooperative_groups;
+
 namespace wgb {
 namespace {
 
-constexpr int kKT = 32;       // keys per shared-memory tile
+constexpr int kKT = 64;        // keys per shared-memory tile (FAST)
 constexpr int kThreads = 256;
-constexpr int kMaxAcc = 8;    // output accumulators per thread (HPC*dv <= 2048)
+constexpr int kMaxAcc = 8;     // output accumulators per thread (HPC*dv <= 2048)
+constexpr int kMaxCluster = 8; // portable cluster size
+constexpr int kRefChunk = 128; // keys per shared-memory chunk (REFERENCE)
+constexpr int kRefSmemScores = 11000;  // scores kept in shared memory (REFERENCE)
 
 struct AttnShape {
-    int S, nh, nkvh, d, dv, L, hpc, nsplit, keys_per_split;
+    int S, nh, nkvh, d, dv, L, hpc, nsplit;
     float scale;
 };
 
@@ -53,9 +64,9 @@ template <typename T> struct KvDense {
     }
 };
 
-// KvCache: batched decode. Query row b is the newest token of sequence
-// seq0 + b, whose cache holds lens[b] + 1 positions (its own K/V included);
-// it sees all of them.
+// KvCache: batched decode. Query row b is the newest token of sequence b,
+// whose cache holds lens[b] + 1 positions (its own K/V included); it sees
+// all of them.
 template <typename T> struct KvCache {
     const T *k, *v;          // cache of sequence 0
     size_t seq_stride;       // elements between consecutive sequences
@@ -73,32 +84,84 @@ template <typename T> struct KvCache {
     }
 };
 
-template <typename T, class Src>
-__global__ void __launch_bounds__(kThreads) attn_split_kernel(const T *__restrict__ q, Src src, T *__restrict__ out,
-                                                              float *__restrict__ ws, AttnShape sh) {
-    extern __shared__ float smem[];
-    const int dp = sh.d + 1, dvp = sh.dv + 1;
-    float *qs = smem;                          // [hpc][d]
-    float *ks = qs + sh.hpc * sh.d;            // [kKT][d+1]
-    float *vs = ks + kKT * dp;                 // [kKT][dv+1]
-    float *ps = vs + kKT * dvp;                // [hpc][kKT]
-    float *mrow = ps + sh.hpc * kKT;           // [hpc] running max
-    float *lrow = mrow + sh.hpc;               // [hpc] running sum
-    float *corr = lrow + sh.hpc;               // [hpc] rescale for this tile
+// Copies rows [0, nrows) of a [rows][width] tile (row r at src + r * gstride
+// elements) into shared memory with row stride sstride elements. kVec: 16-byte
+// cp.async chunks (width * size and both strides 16-byte multiples, src
+// 16-byte aligned); otherwise element copies.
+template <typename T, bool kVec>
+__device__ __forceinline__ void load_tile(T *dst, const T *src, int nrows, int width, size_t gstride, int sstride) {
+    if (kVec) {
+        constexpr int V = 16 / sizeof(T);
+        const int cpr = width / V;
+        for (int c = threadIdx.x; c < nrows * cpr; c += kThreads) {
+            const int r = c / cpr, cc = c - r * cpr;
+            __pipeline_memcpy_async(dst + (size_t)r * sstride + cc * V, src + (size_t)r * gstride + cc * V, 16);
+        }
+    } else {
+        for (int c = threadIdx.x; c < nrows * width; c += kThreads) {
+            const int r = c / width, cc = c - r * width;
+            dst[(size_t)r * sstride + cc] = src[(size_t)r * gstride + cc];
+        }
+    }
+}
 
+struct FastSmem {
+    int qs, kt, vt, ps, stat, xml, xo, bytes;  // byte offsets
+};
+
+__host__ __device__ inline int pad_row(int width, int es) { return width + 16 / es; }
+
+__host__ __device__ inline FastSmem fast_smem(const AttnShape &sh, int es) {
+    FastSmem f;
+    int o = 0;
+    f.qs = o; o += sh.hpc * sh.d * 4;
+    o = (o + 15) & ~15;
+    f.kt = o; o += 2 * kKT * pad_row(sh.d, es) * es;
+    f.vt = o; o += 2 * kKT * pad_row(sh.dv, es) * es;
+    f.ps = o; o += sh.hpc * kKT * 4;
+    f.stat = o; o += 3 * 8 * 4;           // m, l, corr for up to 8 heads
+    f.xml = o; o += 2 * kMaxCluster * 8 * 4;               // every slice's (m, l) per head, on CTA 0
+    f.xo = o; o += sh.nsplit * sh.hpc * sh.dv * 4;         // every slice's partial output, on CTA 0
+    f.bytes = o;
+    return f;
+}
+
+template <typename T, class Src, bool kVec>
+__global__ void __launch_bounds__(kThreads) attn_fast_kernel(const T *__restrict__ q, Src src, T *__restrict__ out,
+                                                             AttnShape sh) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    constexpr int es = sizeof(T);
+    const FastSmem lay = fast_smem(sh, es);
+    float *qs = reinterpret_cast<float *>(smem + lay.qs);
+    T *kt = reinterpret_cast<T *>(smem + lay.kt);
+    T *vt = reinterpret_cast<T *>(smem + lay.vt);
+    float *ps = reinterpret_cast<float *>(smem + lay.ps);
+    float *mrow = reinterpret_cast<float *>(smem + lay.stat);
+    float *lrow = mrow + 8, *corr = mrow + 16;
+    float *xm = reinterpret_cast<float *>(smem + lay.xml);  // [kMaxCluster][8]
+    float *xl = xm + kMaxCluster * 8;                        // [kMaxCluster][8]
+    float *xo = reinterpret_cast<float *>(smem + lay.xo);    // [nsplit][hpc * dv]
+    const int kst = pad_row(sh.d, es), vst = pad_row(sh.dv, es);
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int nsplit = (int)cluster.num_blocks();
     const int hblocks = sh.nh / sh.hpc;
     const int i = blockIdx.y / hblocks;
-    const int hb = blockIdx.y % hblocks;
-    const int h0 = hb * sh.hpc;
+    const int h0 = (blockIdx.y % hblocks) * sh.hpc;
     const int kvh = h0 * sh.nkvh / sh.nh;
-    const int split = blockIdx.x;
+    const int tid = threadIdx.x;
+    pdl_trigger();
+    pdl_wait();  // q and the cache are written by the previous kernel
     const T *k, *v;
     int nkeys, nvis;
     bool uniform;
     src.row(sh, i, k, v, nkeys, nvis, uniform);
-    const int j0 = split * sh.keys_per_split;
-    const int j1 = min(j0 + sh.keys_per_split, nvis);
-    const int tid = threadIdx.x;
+    const int tiles = (nvis + kKT - 1) / kKT;
+    const int per = (tiles + nsplit - 1) / nsplit;
+    const int j0 = min(rank * per * kKT, nvis), j1 = min((rank + 1) * per * kKT, nvis);
+    const size_t kstride = (size_t)sh.nkvh * sh.d, vstride = (size_t)sh.nkvh * sh.dv;
+    const T *kb = k + (size_t)kvh * sh.d, *vb = v + (size_t)kvh * sh.dv;
 
     for (int x = tid; x < sh.hpc * sh.d; x += kThreads) {
         const int hh = x / sh.d, c = x - hh * sh.d;
@@ -112,147 +175,364 @@ __global__ void __launch_bounds__(kThreads) attn_split_kernel(const T *__restric
 #pragma unroll
     for (int a = 0; a < kMaxAcc; a++) acc[a] = 0.f;
     const int nacc = sh.hpc * sh.dv;
-    __syncthreads();
+    const int kgroups = nacc >= kThreads ? 1 : kThreads / nacc;  // key groups per output column
 
-    for (int t0 = j0; t0 < j1; t0 += kKT) {
+    auto issue = [&](int t0, int buf) {
         const int nt = min(kKT, j1 - t0);
-        for (int x = tid; x < nt * sh.d; x += kThreads) {
-            const int jj = x / sh.d, c = x - jj * sh.d;
-            ks[jj * dp + c] = ldf(k, ((size_t)(t0 + jj) * sh.nkvh + kvh) * sh.d + c);
-        }
-        for (int x = tid; x < nt * sh.dv; x += kThreads) {
-            const int jj = x / sh.dv, c = x - jj * sh.dv;
-            vs[jj * dvp + c] = ldf(v, ((size_t)(t0 + jj) * sh.nkvh + kvh) * sh.dv + c);
+        load_tile<T, kVec>(kt + (size_t)buf * kKT * kst, kb + (size_t)t0 * kstride, nt, sh.d, kstride, kst);
+        load_tile<T, kVec>(vt + (size_t)buf * kKT * vst, vb + (size_t)t0 * vstride, nt, sh.dv, vstride, vst);
+        __pipeline_commit();
+    };
+    if (j0 < j1) issue(j0, 0);
+    int buf = 0;
+    for (int t0 = j0; t0 < j1; t0 += kKT, buf ^= 1) {
+        const int nt = min(kKT, j1 - t0);
+        if (t0 + kKT < j1) {
+            issue(t0 + kKT, buf ^ 1);
+            __pipeline_wait_prior(1);
+        } else {
+            __pipeline_wait_prior(0);
         }
         __syncthreads();
-        // scores for hpc x nt
-        for (int x = tid; x < sh.hpc * kKT; x += kThreads) {
-            const int hh = x / kKT, jj = x - hh * kKT;
-            float sc = -FLT_MAX;
-            if (jj < nt) {
-                if (uniform) {
-                    sc = 0.f;
-                } else {
-                    const float *qq = qs + hh * sh.d;
-                    const float *kk = ks + jj * dp;
-                    float a = 0.f;
-                    for (int c = 0; c < sh.d; c++) a = fmaf(qq[c], kk[c], a);
-                    sc = sh.scale * a;
+        const T *K = kt + (size_t)buf * kKT * kst;
+        const T *Vt = vt + (size_t)buf * kKT * vst;
+        // scores: 4 threads per key, each a quarter of the dot for every head
+        {
+            const int jj = tid >> 2, qd = tid & 3;
+            float part[8];
+#pragma unroll
+            for (int hh = 0; hh < 8; hh++) part[hh] = 0.f;
+            if (jj < nt && !uniform) {
+                const int q0 = qd * (sh.d / 4), q1 = (qd == 3) ? sh.d : q0 + sh.d / 4;
+                const T *kr = K + (size_t)jj * kst;
+                for (int c = q0; c < q1; c++) {
+                    const float kv = Elem<T>::load(kr[c]);
+#pragma unroll
+                    for (int hh = 0; hh < 8; hh++)
+                        if (hh < sh.hpc) part[hh] = fmaf(qs[hh * sh.d + c], kv, part[hh]);
                 }
             }
-            ps[x] = sc;
-        }
-        __syncthreads();
-        // online softmax update: one warp per head
-        const int warp = tid >> 5, lane = tid & 31;
-        for (int hh = warp; hh < sh.hpc; hh += kThreads / 32) {
-            float sc = lane < nt ? ps[hh * kKT + lane] : -FLT_MAX;
-            float mt = warp_max(sc);
-            float mold = mrow[hh];
-            float mnew = fmaxf(mold, mt);
-            float p = lane < nt ? __expf(sc - mnew) : 0.f;
-            ps[hh * kKT + lane] = p;
-            float sp = warp_sum(p);
-            if (lane == 0) {
-                float c = __expf(mold - mnew);
-                corr[hh] = c;
-                lrow[hh] = lrow[hh] * c + sp;
-                mrow[hh] = mnew;
+#pragma unroll
+            for (int hh = 0; hh < 8; hh++) {
+                part[hh] += __shfl_xor_sync(0xffffffffu, part[hh], 1);
+                part[hh] += __shfl_xor_sync(0xffffffffu, part[hh], 2);
+            }
+            if (qd == 0 && jj < kKT) {
+#pragma unroll
+                for (int hh = 0; hh < 8; hh++)
+                    if (hh < sh.hpc) ps[hh * kKT + jj] = jj < nt ? (uniform ? 0.f : sh.scale * part[hh]) : -FLT_MAX;
             }
         }
         __syncthreads();
+        // online softmax: one warp per head, two keys per lane
+        {
+            const int warp = tid >> 5, lane = tid & 31;
+            for (int hh = warp; hh < sh.hpc; hh += kThreads / 32) {
+                const float s0 = ps[hh * kKT + lane], s1 = ps[hh * kKT + lane + 32];
+                const float mt = warp_max(fmaxf(s0, s1));
+                const float mold = mrow[hh];
+                const float mnew = fmaxf(mold, mt);
+                const float p0 = lane < nt ? __expf(s0 - mnew) : 0.f;
+                const float p1 = lane + 32 < nt ? __expf(s1 - mnew) : 0.f;
+                ps[hh * kKT + lane] = p0;
+                ps[hh * kKT + lane + 32] = p1;
+                const float sp = warp_sum(p0 + p1);
+                if (lane == 0) {
+                    const float c = __expf(mold - mnew);
+                    corr[hh] = c;
+                    lrow[hh] = lrow[hh] * c + sp;
+                    mrow[hh] = mnew;
+                }
+            }
+        }
+        __syncthreads();
+        // P.V: when hpc*dv < threads, kgroups threads share a column, each
+        // taking every kgroups-th key; their partials meet after the last tile
 #pragma unroll
         for (int a = 0; a < kMaxAcc; a++) {
             const int x = tid + a * kThreads;
-            if (x < nacc) {
-                const int hh = x / sh.dv, c = x - hh * sh.dv;
-                float s = acc[a] * corr[hh];
+            if (x < nacc * kgroups) {
+                const int col = x % nacc, grp = x / nacc;
+                const int hh = col / sh.dv, c = col - hh * sh.dv;
+                float sacc = acc[a] * corr[hh];
                 const float *pp = ps + hh * kKT;
-                for (int jj = 0; jj < nt; jj++) s = fmaf(pp[jj], vs[jj * dvp + c], s);
-                acc[a] = s;
+                const T *vc = Vt + c;
+#pragma unroll 4
+                for (int jj = grp; jj < nt; jj += kgroups) sacc = fmaf(pp[jj], Elem<T>::load(vc[(size_t)jj * vst]), sacc);
+                acc[a] = sacc;
             }
         }
         __syncthreads();
     }
-
-    if (sh.nsplit == 1) {
+    if (kgroups > 1) {  // fold the key groups: group 0 keeps the column sums
+        float *fold = reinterpret_cast<float *>(smem + lay.kt);  // the K tile buffer is free now
 #pragma unroll
         for (int a = 0; a < kMaxAcc; a++) {
             const int x = tid + a * kThreads;
-            if (x < nacc) {
-                const int hh = x / sh.dv, c = x - hh * sh.dv;
-                const float l = lrow[hh];
-                stf(out, ((size_t)i * sh.nh + h0 + hh) * sh.dv + c, l > 0.f ? acc[a] / l : 0.f);
-            }
+            if (x < nacc * kgroups && x >= nacc) fold[x] = acc[a];
         }
-        return;
-    }
-    // workspace: ml[S][nh][nsplit][2], o[S][nh][nsplit][dv]
-    float *ml = ws;
-    float *o = ws + (size_t)sh.S * sh.nh * sh.nsplit * 2;
-    if (tid < sh.hpc) {
-        const size_t r = ((size_t)i * sh.nh + h0 + tid) * sh.nsplit + split;
-        ml[r * 2] = j0 < j1 ? mrow[tid] : -FLT_MAX;
-        ml[r * 2 + 1] = lrow[tid];
-    }
+        __syncthreads();
 #pragma unroll
-    for (int a = 0; a < kMaxAcc; a++) {
-        const int x = tid + a * kThreads;
-        if (x < nacc) {
+        for (int a = 0; a < kMaxAcc; a++) {
+            const int x = tid + a * kThreads;
+            if (x < nacc)
+                for (int gidx = 1; gidx < kgroups; gidx++) acc[a] += fold[x + gidx * nacc];
+        }
+    }
+    // publish this slice into CTA 0's shared memory (remote stores do not
+    // stall), then CTA 0 folds the slices from its own shared memory
+    if (j0 >= j1 && tid < sh.hpc) {
+        mrow[tid] = -FLT_MAX;
+        lrow[tid] = 0.f;
+    }
+    __syncthreads();
+    {
+        float *dxo = cluster.map_shared_rank(xo, 0) + (size_t)rank * nacc;
+#pragma unroll
+        for (int a = 0; a < kMaxAcc; a++) {
+            const int x = tid + a * kThreads;
+            if (x < nacc) dxo[x] = acc[a];
+        }
+        if (tid < sh.hpc) {
+            cluster.map_shared_rank(xm, 0)[rank * 8 + tid] = mrow[tid];
+            cluster.map_shared_rank(xl, 0)[rank * 8 + tid] = lrow[tid];
+        }
+    }
+    cluster.sync();
+    if (rank == 0) {
+        for (int x = tid; x < nacc; x += kThreads) {
             const int hh = x / sh.dv, c = x - hh * sh.dv;
-            o[(((size_t)i * sh.nh + h0 + hh) * sh.nsplit + split) * sh.dv + c] = acc[a];
+            float M = -FLT_MAX;
+            for (int r = 0; r < nsplit; r++) M = fmaxf(M, xm[r * 8 + hh]);
+            float L = 0.f, O = 0.f;
+            for (int r = 0; r < nsplit; r++) {
+                const float l = xl[r * 8 + hh];
+                if (l > 0.f) {
+                    const float w = __expf(xm[r * 8 + hh] - M);
+                    L += l * w;
+                    O += xo[(size_t)r * nacc + x] * w;
+                }
+            }
+            stf(out, ((size_t)i * sh.nh + h0 + hh) * sh.dv + c, L > 0.f ? O / L : 0.f);
         }
     }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(128) attn_combine_kernel(const float *__restrict__ ws, T *__restrict__ out,
-                                                           AttnShape sh) {
-    const int row = blockIdx.x;  // i * nh + h
-    const float *ml = ws + (size_t)row * sh.nsplit * 2;
-    const float *o = ws + (size_t)sh.S * sh.nh * sh.nsplit * 2 + (size_t)row * sh.nsplit * sh.dv;
-    float M = -FLT_MAX;
-    for (int s = 0; s < sh.nsplit; s++) M = fmaxf(M, ml[2 * s]);
-    float L = 0.f;
-    for (int s = 0; s < sh.nsplit; s++)
-        if (ml[2 * s + 1] > 0.f) L += ml[2 * s + 1] * __expf(ml[2 * s] - M);
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    for (int c = threadIdx.x; c < sh.dv; c += blockDim.x) {
-        float a = 0.f;
-        for (int s = 0; s < sh.nsplit; s++)
-            if (ml[2 * s + 1] > 0.f) a += o[(size_t)s * sh.dv + c] * __expf(ml[2 * s] - M);
-        stf(out, (size_t)row * sh.dv + c, a * inv);
+// ---- FAST, one head per warp (decode and short query blocks) ---------------
+// Lane j of a warp owns key j of a 32-key chunk and computes its whole dot
+// product from registers (the K row is one coalesced 256-byte read per lane
+// pair of 16-byte vectors), so the score phase has no shared-memory traffic
+// and no block barrier. The warp then folds the chunk into its running
+// (max, sum, output) with shuffles, and for P.V each lane owns DH/32 output
+// columns: V rows are read coalesced across the warp, the weight of key j
+// is broadcast by shuffle. Warps of a CTA take interleaved chunks of the
+// CTA's key slice; the 8 warps, then the cluster's CTAs, are folded in
+// shared memory (the cluster's slices are pushed into CTA 0).
+constexpr int kWarpKeys = 32;
+
+template <typename T, int DH, class Src>
+__global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict__ q, Src src, T *__restrict__ out, AttnShape sh,
+                                                             const void *pf_ptr, size_t pf_bytes) {
+    constexpr int V = 16 / sizeof(T);        // elements per 16-byte vector
+    constexpr int NV = DH / V;                // vectors per row
+    constexpr int CPL = DH / 32;              // output columns per lane
+    __shared__ __align__(16) float qs[DH];
+    __shared__ float wm[8], wl[8];
+    __shared__ __align__(16) float wo[8][DH];
+    __shared__ float xm[kMaxCluster], xl[kMaxCluster];
+    __shared__ __align__(16) float xo[kMaxCluster][DH];
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int nsplit = (int)cluster.num_blocks();
+    const int i = blockIdx.y / sh.nh, h = blockIdx.y % sh.nh;
+    const int kvh = h * sh.nkvh / sh.nh;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const T *k, *v;
+    int nkeys, nvis;
+    bool uniform;
+    src.row(sh, i, k, v, nkeys, nvis, uniform);  // lengths were set by an earlier step
+    const int chunks = (nvis + kWarpKeys - 1) / kWarpKeys;
+    const int per = (chunks + nsplit - 1) / nsplit;
+    const int c0 = rank * per, c1 = min(c0 + per, chunks);
+    const size_t kst = (size_t)sh.nkvh * DH;
+    const T *kb = k + (size_t)kvh * DH, *vb = v + (size_t)kvh * DH;
+    // Older cache rows are not touched by the previous kernel (it appends
+    // one row): start pulling this CTA's slice into L2 before waiting.
+    if (threadIdx.x == 0 && c0 < c1) {
+        const int r0 = c0 * kWarpKeys, r1 = min(c1 * kWarpKeys, nvis) - 1;  // rows [r0, r1) predate this step
+        if (r1 > r0) {
+            const uint32_t bytes = (uint32_t)((size_t)(r1 - r0) * kst * sizeof(T));
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(k + (size_t)r0 * kst), "r"(bytes) : "memory");
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(v + (size_t)r0 * kst), "r"(bytes) : "memory");
+        }
     }
+    if (threadIdx.x == 32)  // the next kernel's weights stream into L2 meanwhile
+        l2_prefetch_share(pf_ptr, pf_bytes, blockIdx.x + gridDim.x * blockIdx.y, gridDim.x * gridDim.y);
+    pdl_trigger();
+    pdl_wait();  // q and the newest cache row are written by the previous kernel
+    for (int c = threadIdx.x; c < DH; c += kThreads) qs[c] = ldf(q, ((size_t)i * sh.nh + h) * DH + c);
+    __syncthreads();
+
+    float m = -FLT_MAX, l = 0.f;
+    float o[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; c++) o[c] = 0.f;
+
+    for (int ch = c0 + warp; ch < c1; ch += 8) {
+        const int j = ch * kWarpKeys + lane;
+        const bool ok = j < nvis;
+        float sc = -FLT_MAX;
+        if (ok) {
+            const uint4 *kr = reinterpret_cast<const uint4 *>(kb + (size_t)j * kst);
+            Vec16<T> kv[NV];
+#pragma unroll
+            for (int u = 0; u < NV; u++) kv[u].u = kr[u];
+            float dot = 0.f;
+#pragma unroll
+            for (int u = 0; u < NV; u++)
+#pragma unroll
+                for (int e = 0; e < V; e++) dot = fmaf(qs[u * V + e], Elem<T>::load(kv[u].e[e]), dot);
+            sc = uniform ? 0.f : sh.scale * dot;
+        }
+        const float mnew = fmaxf(m, warp_max(sc));
+        const float p = ok ? __expf(sc - mnew) : 0.f;
+        const float corr = __expf(m - mnew);
+        l = l * corr + warp_sum(p);
+        m = mnew;
+#pragma unroll
+        for (int c = 0; c < CPL; c++) o[c] *= corr;
+        const int nk = min(kWarpKeys, nvis - ch * kWarpKeys);
+        const T *vr = vb + (size_t)(ch * kWarpKeys) * kst + lane * CPL;
+#pragma unroll 8
+        for (int jj = 0; jj < nk; jj++) {
+            const float pj = __shfl_sync(0xffffffffu, p, jj);
+            const T *vv = vr + (size_t)jj * kst;
+            T vl[CPL];
+            if constexpr (CPL * sizeof(T) == 16) {
+                *reinterpret_cast<uint4 *>(vl) = *reinterpret_cast<const uint4 *>(vv);
+            } else if constexpr (CPL * sizeof(T) == 8) {
+                *reinterpret_cast<uint2 *>(vl) = *reinterpret_cast<const uint2 *>(vv);
+            } else if constexpr (CPL * sizeof(T) == 4) {
+                *reinterpret_cast<uint32_t *>(vl) = *reinterpret_cast<const uint32_t *>(vv);
+            } else {
+#pragma unroll
+                for (int c = 0; c < CPL; c++) vl[c] = vv[c];
+            }
+#pragma unroll
+            for (int c = 0; c < CPL; c++) o[c] = fmaf(pj, Elem<T>::load(vl[c]), o[c]);
+        }
+    }
+    // fold the 8 warps
+    if (lane == 0) {
+        wm[warp] = m;
+        wl[warp] = l;
+    }
+#pragma unroll
+    for (int c = 0; c < CPL; c++) wo[warp][lane * CPL + c] = o[c];
+    __syncthreads();
+    float M = -FLT_MAX;
+#pragma unroll
+    for (int w = 0; w < 8; w++) M = fmaxf(M, wm[w]);
+    float Lsum = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) Lsum += wl[w] > 0.f ? wl[w] * __expf(wm[w] - M) : 0.f;
+    // one column per thread (DH <= 256 threads); push the CTA's slice to CTA 0
+    float oc = 0.f;
+    if (threadIdx.x < DH) {
+#pragma unroll
+        for (int w = 0; w < 8; w++)
+            if (wl[w] > 0.f) oc += wo[w][threadIdx.x] * __expf(wm[w] - M);
+        cluster.map_shared_rank(&xo[0][0], 0)[rank * DH + threadIdx.x] = oc;
+    }
+    if (threadIdx.x == 0) {
+        cluster.map_shared_rank(xm, 0)[rank] = M;
+        cluster.map_shared_rank(xl, 0)[rank] = Lsum;
+    }
+    cluster.sync();
+    if (rank == 0 && threadIdx.x < DH) {
+        float MM = -FLT_MAX;
+        for (int r = 0; r < nsplit; r++) MM = fmaxf(MM, xm[r]);
+        float LL = 0.f, OO = 0.f;
+        for (int r = 0; r < nsplit; r++)
+            if (xl[r] > 0.f) {
+                const float w = __expf(xm[r] - MM);
+                LL += xl[r] * w;
+                OO += xo[r][threadIdx.x] * w;
+            }
+        stf(out, ((size_t)i * sh.nh + h) * DH + threadIdx.x, LL > 0.f ? OO / LL : 0.f);
+    }
+}
+
+template <typename T, int DH, class Src>
+int launch_warp_attn(T *out, const T *q, Src src, const AttnShape &sh, cudaStream_t s, const void *pf_ptr,
+                     size_t pf_bytes) {
+    // slices: enough CTAs per head to give each warp about one 32-key chunk
+    const int chunks = (sh.L + kWarpKeys - 1) / kWarpKeys;
+    int ns = (chunks + 7) / 8;
+    if (ns > kMaxCluster) ns = kMaxCluster;
+    if (ns < 1) ns = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ns, (unsigned)(sh.S * sh.nh), 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)ns;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_warp_kernel<T, DH, Src>, q, src, out, sh, pf_ptr, pf_bytes);
+    if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "self_attention(warp): %s", cudaGetErrorString(e));
+    return check_launch("self_attention(warp)");
 }
 
 // ---- REFERENCE order --------------------------------------------------------
-template <typename T, class Src>
+template <typename T, class Src, bool kVec>
 __global__ void __launch_bounds__(kThreads) attn_ref_kernel(const T *__restrict__ q, Src src, T *__restrict__ out,
                                                             float *__restrict__ gscores, AttnShape sh) {
-    extern __shared__ float smem[];
+    extern __shared__ __align__(16) unsigned char smem[];
     __shared__ float s_red[kThreads / 32];
     __shared__ float s_max, s_sum;
+    constexpr int es = sizeof(T);
     const int i = blockIdx.x / sh.nh, h = blockIdx.x % sh.nh;
     const int kvh = h * sh.nkvh / sh.nh;
-    float *qs = smem;  // [d]
-    float *sc = gscores ? gscores + (size_t)blockIdx.x * sh.L : smem + sh.d;  // [L]
+    const int wmax = sh.d > sh.dv ? sh.d : sh.dv;
+    const int rst = pad_row(wmax, es);  // shared row stride (elements)
+    float *qs = reinterpret_cast<float *>(smem);
+    T *tile = reinterpret_cast<T *>(smem + ((sh.d * 4 + 15) & ~15));
+    float *sc = gscores ? gscores + (size_t)blockIdx.x * sh.L
+                        : reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(tile) + (size_t)kRefChunk * rst * es);
     const int tid = threadIdx.x;
     const T *k, *v;
     int nkeys, nvis;
     bool uniform;
     src.row(sh, i, k, v, nkeys, nvis, uniform);
+    const size_t kstride = (size_t)sh.nkvh * sh.d, vstride = (size_t)sh.nkvh * sh.dv;
+    const T *kb = k + (size_t)kvh * sh.d, *vb = v + (size_t)kvh * sh.dv;
     for (int c = tid; c < sh.d; c += kThreads) qs[c] = ldf(q, ((size_t)i * sh.nh + h) * sh.d + c);
-    __syncthreads();
+    // masked / uniform keys first (no dot product needed)
+    for (int j = tid; j < nkeys; j += kThreads)
+        if (uniform || j >= nvis) sc[j] = -1e9f;
     // scores: sequential dot, then scale * dot (self_attention_cpu.cpp:37-45)
-    for (int j = tid; j < nkeys; j += kThreads) {
-        float s = -1e9f;
-        if (!uniform && j < nvis) {
-            const T *kk = k + ((size_t)j * sh.nkvh + kvh) * sh.d;
+    const int nscore = uniform ? 0 : nvis;
+    for (int c0 = 0; c0 < nscore; c0 += kRefChunk) {
+        const int nc = min(kRefChunk, nscore - c0);
+        __syncthreads();
+        load_tile<T, kVec>(tile, kb + (size_t)c0 * kstride, nc, sh.d, kstride, rst);
+        __pipeline_commit();
+        __pipeline_wait_prior(0);
+        __syncthreads();
+        if (tid < nc) {
+            const T *kr = tile + (size_t)tid * rst;
             float a = 0.f;
-            for (int c = 0; c < sh.d; c++) a = __fadd_rn(a, __fmul_rn(qs[c], ldf(kk, c)));
-            s = __fmul_rn(sh.scale, a);
+            for (int c = 0; c < sh.d; c++) a = __fadd_rn(a, __fmul_rn(qs[c], Elem<T>::load(kr[c])));
+            sc[c0 + tid] = __fmul_rn(sh.scale, a);
         }
-        sc[j] = s;
     }
     __syncthreads();
     float mx = -FLT_MAX;
@@ -277,23 +557,48 @@ __global__ void __launch_bounds__(kThreads) attn_ref_kernel(const T *__restrict_
     __syncthreads();
     const float sum = s_sum;
     for (int j = tid; j < nkeys; j += kThreads) sc[j] = __fdiv_rn(sc[j], sum);
-    __syncthreads();
-    // masked keys carry exact zeros and leave the sums unchanged; skip them
-    const int jend = nvis;
-    for (int c = tid; c < sh.dv; c += kThreads) {
-        const T *vv = v + (size_t)kvh * sh.dv + c;
-        const size_t vstride = (size_t)sh.nkvh * sh.dv;
-        float a = 0.f;
-        for (int j = 0; j < jend; j++) a = __fadd_rn(a, __fmul_rn(sc[j], ldf(vv, (size_t)j * vstride)));
-        stf(out, ((size_t)i * sh.nh + h) * sh.dv + c, a);
+    // output: sequential sum over keys of round(p * v). Masked keys carry
+    // exact zeros and leave the sum unchanged, so the chain stops at nvis.
+    float a[4] = {0.f, 0.f, 0.f, 0.f};  // columns tid, tid+256, ... (dv <= 1024)
+    for (int c0 = 0; c0 < nvis; c0 += kRefChunk) {
+        const int nc = min(kRefChunk, nvis - c0);
+        __syncthreads();
+        load_tile<T, kVec>(tile, vb + (size_t)c0 * vstride, nc, sh.dv, vstride, rst);
+        __pipeline_commit();
+        __pipeline_wait_prior(0);
+        __syncthreads();
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int c = tid + u * kThreads;
+            if (c < sh.dv) {
+                float acc = a[u];
+                for (int jj = 0; jj < nc; jj++)
+                    acc = __fadd_rn(acc, __fmul_rn(sc[c0 + jj], Elem<T>::load(tile[(size_t)jj * rst + c])));
+                a[u] = acc;
+            }
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const int c = tid + u * kThreads;
+        if (c < sh.dv) stf(out, ((size_t)i * sh.nh + h) * sh.dv + c, a[u]);
     }
 }
 
-constexpr int kRefSmemScores = 11000;  // floats of scores kept in shared memory
+size_t ref_smem_bytes(const AttnShape &sh, int es, bool global_scores) {
+    const int wmax = sh.d > sh.dv ? sh.d : sh.dv;
+    size_t b = (size_t)((sh.d * 4 + 15) & ~15) + (size_t)kRefChunk * pad_row(wmax, es) * es;
+    if (!global_scores) b += (size_t)sh.L * 4;
+    return b;
+}
 
-int pick_hpc(int G, int dv) {
+// Heads per CTA: all heads of a kv group (up to 8) share each K/V tile when
+// there are enough query rows to fill the GPU; with few rows (decode) one
+// head per CTA gives 6x more CTAs and keeps each CTA's serial work short.
+int pick_hpc(int G, int dv, long rows_x_heads) {
+    if (rows_x_heads < 2L * sm_count()) return 1;
     for (int h = (G < 8 ? G : 8); h >= 1; h--)
-        if (G % h == 0 && h * dv <= kMaxAcc * kThreads && h * kKT <= kThreads) return h;
+        if (G % h == 0 && h * dv <= kMaxAcc * kThreads) return h;
     return 1;
 }
 
@@ -306,33 +611,33 @@ AttnShape make_shape(size_t S, size_t nh, size_t nkvh, size_t d, size_t dv, size
     sh.dv = (int)dv;
     sh.L = (int)L;
     sh.scale = scale;
-    sh.hpc = pick_hpc((int)(nh / nkvh), (int)dv);
-    const long ctas = (long)S * (long)(nh / sh.hpc);
+    sh.hpc = pick_hpc((int)(nh / nkvh), (int)dv, (long)S * (long)nh);
+    const long rows = (long)S * (long)(nh / sh.hpc);
     const long target = 2L * sm_count();
-    long ns = ctas >= target ? 1 : (target + ctas - 1) / ctas;
-    long max_ns = ((long)L + kKT - 1) / kKT;
-    if (ns > max_ns) ns = max_ns;
-    if (ns < 1) ns = 1;
-    long kps = ((long)L + ns - 1) / ns;
-    kps = (kps + kKT - 1) / kKT * kKT;
-    ns = ((long)L + kps - 1) / kps;
+    long ns = rows >= target ? 1 : (target + rows - 1) / rows;
+    const long tiles = ((long)L + kKT - 1) / kKT;
+    if (ns > tiles) ns = tiles;
+    if (ns > kMaxCluster) ns = kMaxCluster;
     sh.nsplit = (int)(ns < 1 ? 1 : ns);
-    sh.keys_per_split = (int)kps;
     return sh;
 }
 
+// FAST needs no workspace (the cluster folds its slices in shared memory);
+// REFERENCE keeps one score per key in global memory when the cache is too
+// long for shared memory.
 size_t ws_bytes(const AttnShape &sh, bool ref) {
     if (ref) return sh.L > kRefSmemScores ? (size_t)sh.S * sh.nh * sh.L * sizeof(float) : 0;
-    if (sh.nsplit == 1) return 0;
-    return (size_t)sh.S * sh.nh * sh.nsplit * (sh.dv + 2) * sizeof(float);
+    return 0;
 }
 
 // Raises the dynamic shared-memory limits once per device (a non-stream call,
 // kept out of graph capture).
 template <typename T, class Src> void set_attrs() {
-    cudaFuncSetAttribute(attn_ref_kernel<T, Src>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)((1024 + kRefSmemScores) * sizeof(float)));
-    cudaFuncSetAttribute(attn_split_kernel<T, Src>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    const int lim = 200 * 1024;
+    cudaFuncSetAttribute(attn_ref_kernel<T, Src, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(attn_ref_kernel<T, Src, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(attn_fast_kernel<T, Src, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(attn_fast_kernel<T, Src, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
 }
 
 void init_attrs_once() {
@@ -349,22 +654,48 @@ void init_attrs_once() {
     done_mask |= 1ull << dev;
 }
 
+template <typename T> bool vec_ok(const AttnShape &sh, const void *k, const void *v, size_t kstride_bytes_extra = 0) {
+    const int es = sizeof(T);
+    return ((sh.d * es) % 16 == 0) && ((sh.dv * es) % 16 == 0) && aligned16(k) && aligned16(v) &&
+           ((size_t)sh.nkvh * sh.d * es) % 16 == 0 && ((size_t)sh.nkvh * sh.dv * es) % 16 == 0 &&
+           kstride_bytes_extra % 16 == 0;
+}
+
 template <typename T, class Src>
-int launch_attn(T *out, const T *q, Src src, const AttnShape &sh, bool ref, void *ws, cudaStream_t s) {
+int launch_attn(T *out, const T *q, Src src, const AttnShape &sh, bool ref, void *ws, cudaStream_t s, bool vec,
+                const void *pf_ptr = nullptr, size_t pf_bytes = 0) {
     init_attrs_once();
     if (ref) {
-        float *g = sh.L > kRefSmemScores ? (float *)ws : nullptr;
-        size_t smem = (size_t)(sh.d + (g ? 0 : sh.L)) * sizeof(float);
-        attn_ref_kernel<T, Src><<<sh.S * sh.nh, kThreads, smem, s>>>(q, src, out, g, sh);
+        const bool g = sh.L > kRefSmemScores;
+        const size_t smem = ref_smem_bytes(sh, sizeof(T), g);
+        if (vec) attn_ref_kernel<T, Src, true><<<sh.S * sh.nh, kThreads, smem, s>>>(q, src, out, g ? (float *)ws : nullptr, sh);
+        else attn_ref_kernel<T, Src, false><<<sh.S * sh.nh, kThreads, smem, s>>>(q, src, out, g ? (float *)ws : nullptr, sh);
         return check_launch("self_attention(reference)");
     }
-    size_t smem = (size_t)(sh.hpc * sh.d + kKT * (sh.d + 1) + kKT * (sh.dv + 1) + sh.hpc * kKT + 3 * sh.hpc) * sizeof(float);
-    dim3 grid((unsigned)sh.nsplit, (unsigned)(sh.S * (sh.nh / sh.hpc)));
-    attn_split_kernel<T, Src><<<grid, kThreads, smem, s>>>(q, src, out, (float *)ws, sh);
-    int rc = check_launch("self_attention(split)");
-    if (rc || sh.nsplit == 1) return rc;
-    attn_combine_kernel<T><<<sh.S * sh.nh, 128, 0, s>>>((const float *)ws, out, sh);
-    return check_launch("self_attention(combine)");
+    if (vec && sh.d == sh.dv && (sh.d == 128 || sh.d == 64) && (long)sh.S * sh.nh < 2L * sm_count()) {
+        // few query rows: one head per warp-group, no block barriers in the key loop
+        return sh.d == 128 ? launch_warp_attn<T, 128, Src>(out, q, src, sh, s, pf_ptr, pf_bytes)
+                           : launch_warp_attn<T, 64, Src>(out, q, src, sh, s, pf_ptr, pf_bytes);
+    }
+    const FastSmem lay = fast_smem(sh, sizeof(T));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)sh.nsplit, (unsigned)(sh.S * (sh.nh / sh.hpc)), 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)lay.bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)sh.nsplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, attn_fast_kernel<T, Src, true>, q, src, out, sh)
+                        : cudaLaunchKernelEx(&cfg, attn_fast_kernel<T, Src, false>, q, src, out, sh);
+    if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "self_attention(fast): %s", cudaGetErrorString(e));
+    return check_launch("self_attention(fast)");
 }
 
 // Library-owned workspace for the allocation-free-signature entry point.
@@ -375,14 +706,17 @@ struct Workspace {
 thread_local Workspace t_ws[64];
 
 int check_args(const void *o, const void *q, const void *k, const void *v, size_t S, size_t nh, size_t nkvh, size_t d,
-               size_t dv, size_t L) {
+               size_t dv, size_t L, wginferDataType_t dtype) {
     WGB_REQUIRE(o && q && k && v, WGB_ERR_INVALID_ARGUMENT, "wgb_self_attention: null pointer");
     WGB_REQUIRE(nkvh > 0 && nh % nkvh == 0, WGB_ERR_INVALID_ARGUMENT, "wgb_self_attention: nhead %% nkvhead != 0");
-    WGB_REQUIRE(d > 0 && dv > 0 && d <= 512 && dv <= 512, WGB_ERR_INVALID_ARGUMENT,
-                "wgb_self_attention: head dims must be in [1, 512]");
-    WGB_REQUIRE(dv <= (size_t)kMaxAcc * kThreads, WGB_ERR_INVALID_ARGUMENT, "wgb_self_attention: dv too large");
+    const size_t es = dtype == WGINFER_DTYPE_F32 ? 4 : 2;
+    // two double-buffered K/V tiles of kKT keys must fit in shared memory
+    WGB_REQUIRE(d > 0 && dv > 0 && (d + dv) * es <= 1024, WGB_ERR_INVALID_ARGUMENT,
+                "wgb_self_attention: (d + dv) * element size must be <= 1024 bytes (d=%zu, dv=%zu)", d, dv);
     WGB_REQUIRE(S < (1u << 20) && L < (1u << 30) && nh < 4096, WGB_ERR_INVALID_ARGUMENT,
                 "wgb_self_attention: size too large");
+    WGB_REQUIRE(S * nh < 65536u,
+                WGB_ERR_INVALID_ARGUMENT, "wgb_self_attention: too many query rows x heads");
     return WGB_OK;
 }
 
@@ -392,20 +726,20 @@ void attn_prepare() { init_attrs_once(); }
 
 size_t attn_decode_workspace(int B, int nh, int nkvh, int dh, int maxlen, bool ref) {
     AttnShape sh = make_shape((size_t)B, (size_t)nh, (size_t)nkvh, (size_t)dh, (size_t)dh, (size_t)maxlen, 1.f);
-    sh.nsplit = (maxlen + sh.keys_per_split - 1) / sh.keys_per_split;
     return ws_bytes(sh, ref);
 }
 
 int attn_decode(wginferDataType_t dtype, void *out, const void *q, const void *kcache, const void *vcache,
                 size_t seq_stride, const int64_t *lens, int B, int nh, int nkvh, int dh, int maxlen, float scale,
-                void *ws, bool ref, cudaStream_t s) {
-    // The split count depends only on maxlen, so a captured graph stays valid
-    // as the sequences grow; splits past a sequence's length exit at once.
+                void *ws, bool ref, cudaStream_t s, const void *pf_ptr, size_t pf_bytes) {
+    // The cluster size depends only on maxlen, so a captured graph stays valid
+    // as the sequences grow; each row splits its own visible keys.
     AttnShape sh = make_shape((size_t)B, (size_t)nh, (size_t)nkvh, (size_t)dh, (size_t)dh, (size_t)maxlen, scale);
-    sh.nsplit = (maxlen + sh.keys_per_split - 1) / sh.keys_per_split;
     WGB_DISPATCH_FLOAT(dtype, T,
+        const bool vec = vec_ok<T>(sh, kcache, vcache, seq_stride * sizeof(T));
         return launch_attn((T *)out, (const T *)q,
-                           KvCache<T>{(const T *)kcache, (const T *)vcache, seq_stride, lens}, sh, ref, ws, s));
+                           KvCache<T>{(const T *)kcache, (const T *)vcache, seq_stride, lens}, sh, ref, ws, s, vec,
+                           pf_ptr, pf_bytes));
     return WGB_OK;
 }
 
@@ -423,7 +757,7 @@ extern "C" int wgb_self_attention_ex(void *attn_val, const void *q, const void *
                                      size_t dv, size_t total_len, float scale, void *workspace, size_t workspace_bytes,
                                      wginferStream_t stream) {
     if (seqlen == 0 || nhead == 0) return WGB_OK;
-    int rc = wgb::check_args(attn_val, q, k, v, seqlen, nhead, nkvhead, d, dv, total_len);
+    int rc = wgb::check_args(attn_val, q, k, v, seqlen, nhead, nkvhead, d, dv, total_len, dtype);
     if (rc) return rc;
     if (total_len == 0) return wgb::set_error(WGB_ERR_INVALID_ARGUMENT, "wgb_self_attention: total_len == 0");
     const bool ref = wgb::current_numerics() == WGB_NUMERICS_REFERENCE;
@@ -432,8 +766,9 @@ extern "C" int wgb_self_attention_ex(void *attn_val, const void *q, const void *
     WGB_REQUIRE(workspace_bytes >= need && (need == 0 || workspace != nullptr), WGB_ERR_INVALID_ARGUMENT,
                 "wgb_self_attention_ex: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
     WGB_DISPATCH_FLOAT(dtype, T,
+        const bool vec = wgb::vec_ok<T>(sh, k, v);
         return wgb::launch_attn((T *)attn_val, (const T *)q, wgb::KvDense<T>{(const T *)k, (const T *)v}, sh, ref,
-                                workspace, (cudaStream_t)stream));
+                                workspace, (cudaStream_t)stream, vec));
     return WGB_OK;
 }
 
@@ -441,7 +776,7 @@ extern "C" int wgb_self_attention(void *attn_val, const void *q, const void *k, 
                                   size_t seqlen, size_t nhead, size_t nkvhead, size_t d, size_t dv, size_t total_len,
                                   float scale, wginferStream_t stream) {
     if (seqlen == 0 || nhead == 0) return WGB_OK;
-    int rc = wgb::check_args(attn_val, q, k, v, seqlen, nhead, nkvhead, d, dv, total_len);
+    int rc = wgb::check_args(attn_val, q, k, v, seqlen, nhead, nkvhead, d, dv, total_len, dtype);
     if (rc) return rc;
     const size_t need = wgb_self_attention_workspace_size(seqlen, nhead, nkvhead, d, dv, total_len);
     void *ws = nullptr;
@@ -518,7 +853,7 @@ extern "C" int wgb_self_attention_noalloc(void *attn_val, const void *q, const v
                                           size_t d, size_t dv, size_t total_len, float scale,
                                           wginferStream_t stream) {
     if (seqlen == 0 || nhead == 0) return WGB_OK;
-    int rc = wgb::check_args(attn_val, q, k, v, seqlen, nhead, nkvhead, d, dv, total_len);
+    int rc = wgb::check_args(attn_val, q, k, v, seqlen, nhead, nkvhead, d, dv, total_len, dtype);
     if (rc) return rc;
     const size_t need = wgb_self_attention_workspace_size(seqlen, nhead, nkvhead, d, dv, total_len);
     WGB_REQUIRE(need <= wgb::kStaticScratchBytes, WGB_ERR_OUT_OF_RANGE,

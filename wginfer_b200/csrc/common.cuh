@@ -88,6 +88,28 @@ __device__ __forceinline__ float pow_cr(float b, float e) { return (float)pow((d
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Programmatic dependent launch: let the next kernel in the stream launch now,
+// and wait until the previous kernel's results are visible. Both are no-ops
+// for a kernel launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Pulls [p, p + bytes) into L2, this CTA taking its 1/nctas share in
+// 64 KB bulk prefetches (sizes and addresses kept 16-byte granular).
+__device__ __forceinline__ void l2_prefetch_share(const void *p, size_t bytes, int cta, int nctas) {
+    if (p == nullptr || bytes == 0) return;
+    const size_t chunk = 64 * 1024;
+    const size_t nchunks = (bytes + chunk - 1) / chunk;
+    for (size_t c = (size_t)cta; c < nchunks; c += (size_t)nctas) {
+        const size_t off = c * chunk;
+        size_t n = bytes - off < chunk ? bytes - off : chunk;
+        n &= ~(size_t)15;
+        if (n)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((const char *)p + off), "r"((uint32_t)n)
+                         : "memory");
+    }
+}
+
 // Records the first bad value a kernel met ({code, value}) in the library's
 // device error word (status.cu) instead of faulting.
 __device__ __forceinline__ void record_device_error(unsigned long long *rec, int code, long long value) {
@@ -104,6 +126,9 @@ int check_launch(const char *what);
 int current_numerics();
 int sm_count();
 unsigned long long *dev_error_ptr();
+// Whether decode kernels are chained with programmatic dependent launch
+// (default on; WGB_PDL=0 in the environment turns it off).
+bool pdl_enabled();
 }  // namespace wgb
 
 #define WGB_REQUIRE(cond, status, ...)                    \

@@ -1,0 +1,396 @@
+// Fused decode GEMV for the Qwen2 caller (FAST numerics, bf16/f16/f32).
+//
+// One weight-streaming kernel per projection, with the neighbouring
+// elementwise work folded in so that it costs no extra launch and no extra
+// HBM round trip:
+//   prologue  RMS   - the input row is rms-normalised inside every CTA (the
+//                     row is 3 KB and sits in L2): xn = round(x * w * s),
+//                     exactly what a separate rms_norm would write;
+//   epilogue  STORE - round(acc + bias), optionally + residual (the skip
+//                     connection: round(r + round(acc)), model.cpp:436-463);
+//             SWIGLU- the two rows of a warp are gate row j and up row j:
+//                     act[j] = round(u * g / (1 + exp(-g))) of the rounded
+//                     projections (swiglu_cpu.cpp:11);
+//             ROPEKV- the two rows of a warp are rotation partners (j, j+dh/2)
+//                     of one q or k head: the rounded pair is rotated with
+//                     the host-built cos/sin table and written to q_rope or
+//                     straight into the K cache; v rows go to the V cache.
+// Each warp owns two weight rows at a time (chosen by the epilogue's row map)
+// and a 1/KS slice of K; lanes stream 16-byte weight vectors with an L2
+// evict-first policy, several vectors in flight per lane. The grid is
+// persistent (4 CTAs per SM) so the prologue runs once per CTA, and each CTA
+// prefetches its next block of rows into L2 while it works on the current one.
+//
+// Launch: programmatic dependent launch. A CTA first prefetches its weight
+// rows into L2 (cp.async.bulk.prefetch), which does not depend on the
+// previous kernel, then waits for the previous kernel's results
+// (griddepcontrol.wait); it allows the next kernel to launch at once
+// (griddepcontrol.launch_dependents), so launches and weight fetches overlap
+// the previous kernel's tail.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace wgb {
+namespace {
+
+constexpr int kRows = 2;       // weight rows per warp
+constexpr int kMaxMT = 8;      // input rows per launch
+constexpr int kVPL = 6;        // 16-byte vectors in flight per row per lane
+constexpr int kCtasPerSM = 4;  // persistent grid: 32 resident warps per SM
+
+enum Pro { PRO_PLAIN = 0, PRO_RMS = 1 };
+enum Epi { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_ROPEKV = 2 };
+
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+template <int EPI>
+__device__ __forceinline__ void row_map(const DecodeGemvParams &p, int g, int &r0, int &r1) {
+    if (EPI == EPI_SWIGLU) {
+        r0 = g;
+        r1 = p.di + g;
+    } else if (EPI == EPI_ROPEKV) {
+        const int half = p.dh >> 1;
+        const int P = (p.nh + p.nkvh) * half;
+        if (g < P) {
+            const int h = g / half, j = g - h * half;
+            r0 = h * p.dh + j;
+            r1 = r0 + half;
+        } else {
+            r0 = (p.nh + p.nkvh) * p.dh + 2 * (g - P);
+            r1 = r0 + 1;
+        }
+    } else {
+        r0 = 2 * g;
+        r1 = 2 * g + 1;
+    }
+}
+
+template <typename T, int EPI>
+__device__ __forceinline__ void epilogue(const DecodeGemvParams &p, int g, int r0, int r1, bool r1ok, int m, float s0,
+                                         float s1) {
+    const T *bias = reinterpret_cast<const T *>(p.bias);
+    if (bias) {
+        s0 += ldf(bias, r0);
+        if (r1ok) s1 += ldf(bias, r1);
+    }
+    if (EPI == EPI_STORE) {
+        T *out = reinterpret_cast<T *>(p.out);
+        const T *res = reinterpret_cast<const T *>(p.res);
+        const size_t i0 = (size_t)m * p.ldo + r0, i1 = (size_t)m * p.ldo + r1;
+        if (res) {
+            s0 = __fadd_rn(ldf(res, i0), Elem<T>::load(Elem<T>::store(s0)));
+            if (r1ok) s1 = __fadd_rn(ldf(res, i1), Elem<T>::load(Elem<T>::store(s1)));
+        }
+        stf(out, i0, s0);
+        if (r1ok) stf(out, i1, s1);
+    } else if (EPI == EPI_SWIGLU) {
+        const float gg = Elem<T>::load(Elem<T>::store(s0));
+        const float uu = Elem<T>::load(Elem<T>::store(s1));
+        stf(reinterpret_cast<T *>(p.out), (size_t)m * p.ldo + g,
+            __fdiv_rn(__fmul_rn(uu, gg), __fadd_rn(1.0f, expf(-gg))));
+    } else {
+        const int64_t pos = p.pos[m];
+        if (pos < 0 || pos >= p.maxseq) {
+            record_device_error(p.err, 3, pos);
+            return;
+        }
+        const int seq = p.prefill_seq >= 0 ? p.prefill_seq : m;
+        const int half = p.dh >> 1;
+        const int P = (p.nh + p.nkvh) * half;
+        T *kc = reinterpret_cast<T *>(p.kc) + (size_t)seq * p.seq_stride + (size_t)pos * p.nkvh * p.dh;
+        T *vc = reinterpret_cast<T *>(p.vc) + (size_t)seq * p.seq_stride + (size_t)pos * p.nkvh * p.dh;
+        const float a = Elem<T>::load(Elem<T>::store(s0));
+        const float b = Elem<T>::load(Elem<T>::store(s1));
+        if (g < P) {
+            const int h = g / half, j = g - h * half;
+            const float2 cs = p.table[(size_t)pos * half + j];
+            const float o0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+            const float o1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+            T *dst = h < p.nh ? reinterpret_cast<T *>(p.q_out) + ((size_t)m * p.nh + h) * p.dh
+                              : kc + (size_t)(h - p.nh) * p.dh;
+            stf(dst, j, o0);
+            stf(dst, j + half, o1);
+        } else {
+            const int e = 2 * (g - P);
+            stf(vc, e, a);
+            if (r1ok) stf(vc, e + 1, b);
+        }
+    }
+}
+
+template <typename T, int MT, int KS, int PRO, int EPI>
+__global__ void __launch_bounds__(256) decode_gemv_kernel(DecodeGemvParams p) {
+    constexpr int V = Vec16<T>::N;
+    constexpr int GROUPS = 8 / KS;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T *xs = reinterpret_cast<T *>(smem_raw);  // [MT][K] normalised input (PRO_RMS)
+    __shared__ float red[8][kRows][MT];
+    __shared__ float s_scale[MT];
+    __shared__ float s_part[8][MT];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rg = warp / KS, ks = warp % KS;
+    const int K = p.K, M = p.M;
+    const int nblocks = (p.groups + GROUPS - 1) / GROUPS;
+
+    auto prefetch_block = [&](int blk) {
+        const int g = blk * GROUPS + rg;
+        if (blk < nblocks && g < p.groups && ks == 0 && lane == 0) {
+            int r0, r1;
+            row_map<EPI>(p, g, r0, r1);
+            prefetch_l2(reinterpret_cast<const T *>(p.w) + (size_t)r0 * K, (uint32_t)(K * sizeof(T)));
+            if (r1 < p.N) prefetch_l2(reinterpret_cast<const T *>(p.w) + (size_t)r1 * K, (uint32_t)(K * sizeof(T)));
+        }
+    };
+    const uint64_t pol = evict_first_policy();
+    const int nvec = K / V;
+    const int per = (nvec + KS - 1) / KS;
+    const int v0 = ks * per, v1 = min(v0 + per, nvec);
+
+    // The first block's first chunk of weights is requested before waiting
+    // for the previous kernel: weights do not depend on it, so their HBM
+    // round trip overlaps that kernel's tail. Later blocks were prefetched
+    // into L2 one block ahead.
+    Vec16<T> wa[kVPL], wb[kVPL];
+    int blk = blockIdx.x;
+    bool have = false;  // wa/wb hold the first chunk of block blk
+    auto load_chunk = [&](int b, int c0) {
+        const int g = b * GROUPS + rg;
+        if (g >= p.groups) return;
+        int r0, r1;
+        row_map<EPI>(p, g, r0, r1);
+        const T *w0 = reinterpret_cast<const T *>(p.w) + (size_t)r0 * K;
+        const T *w1 = reinterpret_cast<const T *>(p.w) + (size_t)(r1 < p.N ? r1 : r0) * K;
+#pragma unroll
+        for (int u = 0; u < kVPL; u++) {
+            const int vi = c0 + lane + 32 * u;
+            if (vi < v1) {
+                wa[u].u = ld_stream_v4(w0 + (size_t)vi * V, pol);
+                wb[u].u = ld_stream_v4(w1 + (size_t)vi * V, pol);
+            }
+        }
+    };
+    if (blk < nblocks) {
+        load_chunk(blk, v0);
+        have = true;
+    }
+    prefetch_block(blk + gridDim.x);
+    if (threadIdx.x == 0) {  // the next kernels' weights stream into L2 behind this one
+        l2_prefetch_share(p.pf_ptr[0], p.pf_bytes[0], blockIdx.x, gridDim.x);
+        l2_prefetch_share(p.pf_ptr[1], p.pf_bytes[1], blockIdx.x, gridDim.x);
+    }
+    pdl_trigger();
+    pdl_wait();
+    const T *x = reinterpret_cast<const T *>(p.x);
+    if (PRO == PRO_RMS) {
+        // every (persistent) CTA normalises the few input rows once
+        for (int m = 0; m < M; m++) {
+            float ss = 0.f;
+            for (int i = threadIdx.x; i < K; i += 256) {
+                const float f = ldf(x, (size_t)m * K + i);
+                ss = fmaf(f, f, ss);
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) s_part[warp][m] = ss;
+        }
+        __syncthreads();
+        if (threadIdx.x < MT) {
+            float t = 0.f;
+            for (int q = 0; q < 8; q++) t += s_part[q][threadIdx.x];
+            const float mean = __fdiv_rn(t, (float)K);
+            s_scale[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+        }
+        __syncthreads();
+        const T *nw = reinterpret_cast<const T *>(p.norm_w);
+        for (int idx = threadIdx.x; idx < M * K; idx += 256) {
+            const int m = idx / K, i = idx - m * K;
+            xs[idx] = Elem<T>::store(__fmul_rn(__fmul_rn(ldf(x, idx), ldf(nw, i)), s_scale[m]));
+        }
+        __syncthreads();
+        x = xs;
+    }
+    for (; blk < nblocks; blk += gridDim.x) {
+        if (blk != (int)blockIdx.x) prefetch_block(blk + gridDim.x);
+        const int g = blk * GROUPS + rg;
+        const bool gok = g < p.groups;
+        int r0 = 0, r1 = 0;
+        if (gok) row_map<EPI>(p, g, r0, r1);
+        const bool r1ok = gok && r1 < p.N;
+
+        float acc[kRows][MT];
+#pragma unroll
+        for (int r = 0; r < kRows; r++)
+#pragma unroll
+            for (int m = 0; m < MT; m++) acc[r][m] = 0.f;
+        if (gok) {
+            // all of a lane's vectors for both rows are requested before any
+            // is used: up to kVPL per row in one round trip
+            for (int c0 = v0; c0 < v1; c0 += 32 * kVPL) {
+                if (!have) load_chunk(blk, c0);
+                have = false;
+#pragma unroll
+                for (int u = 0; u < kVPL; u++) {
+                    const int vi = c0 + lane + 32 * u;
+                    if (vi < v1) {
+#pragma unroll
+                        for (int m = 0; m < MT; m++) {
+                            if (m < M) {
+                                Vec16<T> xv;
+                                xv.u = *reinterpret_cast<const uint4 *>(x + (size_t)m * K + (size_t)vi * V);
+#pragma unroll
+                                for (int e = 0; e < V; e++) {
+                                    const float xf = Elem<T>::load(xv.e[e]);
+                                    acc[0][m] = fmaf(xf, Elem<T>::load(wa[u].e[e]), acc[0][m]);
+                                    acc[1][m] = fmaf(xf, Elem<T>::load(wb[u].e[e]), acc[1][m]);
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        have = false;
+#pragma unroll
+        for (int r = 0; r < kRows; r++)
+#pragma unroll
+            for (int m = 0; m < MT; m++) acc[r][m] = warp_sum(acc[r][m]);
+        if (KS > 1) {
+            if (lane == 0) {
+#pragma unroll
+                for (int r = 0; r < kRows; r++)
+#pragma unroll
+                    for (int m = 0; m < MT; m++) red[warp][r][m] = acc[r][m];
+            }
+            __syncthreads();
+        }
+        if (gok && ks == 0 && lane < MT && lane < M) {
+            const int m = lane;
+            float s0 = 0.f, s1 = 0.f;
+            if (KS > 1) {
+                for (int q = 0; q < KS; q++) {
+                    s0 += red[warp + q][0][m];
+                    s1 += red[warp + q][1][m];
+                }
+            } else {
+#pragma unroll
+                for (int mm = 0; mm < MT; mm++)
+                    if (mm == m) {
+                        s0 = acc[0][mm];
+                        s1 = acc[1][mm];
+                    }
+            }
+            epilogue<T, EPI>(p, g, r0, r1, r1ok, m, s0, s1);
+        }
+        if (KS > 1) __syncthreads();  // red[] is rewritten by the next block
+    }
+}
+
+template <typename T, int MT, int KS, int PRO, int EPI>
+int launch_one(const DecodeGemvParams &p, cudaStream_t s) {
+    constexpr int GROUPS = 8 / KS;
+    const int nblocks = (p.groups + GROUPS - 1) / GROUPS;
+    const int cap = sm_count() * kCtasPerSM;  // persistent: each CTA loops over weight-row blocks
+    const int blocks = nblocks < cap ? nblocks : cap;
+    const size_t smem = PRO == PRO_RMS ? (size_t)MT * p.K * sizeof(T) : 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, decode_gemv_kernel<T, MT, KS, PRO, EPI>, p);
+    if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "decode_gemv: %s", cudaGetErrorString(e));
+    return WGB_OK;
+}
+
+// K split across KS warps: enough that a lane's share of a row fits one
+// round trip (<= kVPL vectors), and more while the grid would leave SMs idle.
+template <typename T, int MT, int PRO, int EPI>
+int launch_ks(const DecodeGemvParams &p, cudaStream_t s) {
+    const int nvec = p.K / Vec16<T>::N;
+    int ks = 1;
+    while (ks < 8 && (nvec + ks - 1) / ks > 32 * kVPL) ks *= 2;
+    while (ks < 8 && (p.groups + 8 / ks - 1) / (8 / ks) < 2 * sm_count() && (nvec + 2 * ks - 1) / (2 * ks) >= 32)
+        ks *= 2;
+    switch (ks) {
+    case 1: return launch_one<T, MT, 1, PRO, EPI>(p, s);
+    case 2: return launch_one<T, MT, 2, PRO, EPI>(p, s);
+    case 4: return launch_one<T, MT, 4, PRO, EPI>(p, s);
+    default: return launch_one<T, MT, 8, PRO, EPI>(p, s);
+    }
+}
+
+template <typename T, int PRO, int EPI>
+int launch_mt(const DecodeGemvParams &p, cudaStream_t s) {
+    if (p.M <= 1) return launch_ks<T, 1, PRO, EPI>(p, s);
+    if (p.M <= 2) return launch_ks<T, 2, PRO, EPI>(p, s);
+    if (p.M <= 4) return launch_ks<T, 4, PRO, EPI>(p, s);
+    return launch_ks<T, 8, PRO, EPI>(p, s);
+}
+
+template <typename T>
+int dispatch(const DecodeGemvParams &p0, int pro, int epi, cudaStream_t s) {
+    // chunks of up to 8 input rows; each chunk re-reads the weights
+    for (int m0 = 0; m0 < p0.M0; m0 += kMaxMT) {
+        DecodeGemvParams p = p0;
+        p.M = min(kMaxMT, p0.M0 - m0);
+        p.x = reinterpret_cast<const T *>(p0.x) + (size_t)m0 * p0.K;
+        if (p.out) p.out = reinterpret_cast<T *>(p0.out) + (size_t)m0 * p0.ldo;
+        if (p.res) p.res = reinterpret_cast<const T *>(p0.res) + (size_t)m0 * p0.ldo;
+        if (p.q_out) p.q_out = reinterpret_cast<T *>(p0.q_out) + (size_t)m0 * p0.nh * p0.dh;
+        if (p.pos) p.pos = p0.pos + m0;
+        if (p0.prefill_seq < 0) {  // row m is sequence m: shift the cache base
+            if (p.kc) p.kc = reinterpret_cast<T *>(p0.kc) + (size_t)m0 * p0.seq_stride;
+            if (p.vc) p.vc = reinterpret_cast<T *>(p0.vc) + (size_t)m0 * p0.seq_stride;
+        }
+        int rc;
+        if (pro == PRO_RMS && epi == EPI_SWIGLU) rc = launch_mt<T, PRO_RMS, EPI_SWIGLU>(p, s);
+        else if (pro == PRO_RMS && epi == EPI_ROPEKV) rc = launch_mt<T, PRO_RMS, EPI_ROPEKV>(p, s);
+        else if (pro == PRO_RMS && epi == EPI_STORE) rc = launch_mt<T, PRO_RMS, EPI_STORE>(p, s);
+        else if (pro == PRO_PLAIN && epi == EPI_STORE) rc = launch_mt<T, PRO_PLAIN, EPI_STORE>(p, s);
+        else return set_error(WGB_ERR_UNSUPPORTED, "decode_gemv: prologue %d with epilogue %d", pro, epi);
+        if (rc) return rc;
+    }
+    return WGB_OK;
+}
+
+template <typename T, int MT, int PRO, int EPI> void attrs_ks() {
+    const int lim = 200 * 1024;
+    cudaFuncSetAttribute(decode_gemv_kernel<T, MT, 1, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(decode_gemv_kernel<T, MT, 2, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(decode_gemv_kernel<T, MT, 4, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(decode_gemv_kernel<T, MT, 8, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+}
+template <typename T, int PRO, int EPI> void attrs_mt() {
+    attrs_ks<T, 1, PRO, EPI>();
+    attrs_ks<T, 2, PRO, EPI>();
+    attrs_ks<T, 4, PRO, EPI>();
+    attrs_ks<T, 8, PRO, EPI>();
+}
+template <typename T> void attrs_all() {
+    attrs_mt<T, PRO_RMS, EPI_SWIGLU>();
+    attrs_mt<T, PRO_RMS, EPI_ROPEKV>();
+    attrs_mt<T, PRO_RMS, EPI_STORE>();
+    attrs_mt<T, PRO_PLAIN, EPI_STORE>();
+}
+
+}  // namespace
+
+void decode_gemv_prepare() {
+    attrs_all<float>();
+    attrs_all<__nv_bfloat16>();
+    attrs_all<__half>();
+}
+
+int decode_gemv(wginferDataType_t dtype, const DecodeGemvParams &p, int pro, int epi, cudaStream_t s) {
+    WGB_DISPATCH_FLOAT(dtype, T, return dispatch<T>(p, pro, epi, s));
+    return WGB_OK;
+}
+
+}  // namespace wgb

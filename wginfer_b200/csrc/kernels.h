@@ -25,10 +25,41 @@ void attn_prepare();  // call outside graph capture, once per device
 size_t attn_decode_workspace(int B, int nh, int nkvh, int dh, int maxlen, bool ref);
 int attn_decode(wginferDataType_t dtype, void *out, const void *q, const void *kcache, const void *vcache,
                 size_t seq_stride, const int64_t *lens, int B, int nh, int nkvh, int dh, int maxlen, float scale,
-                void *ws, bool ref, cudaStream_t s);
+                void *ws, bool ref, cudaStream_t s, const void *pf_ptr = nullptr, size_t pf_bytes = 0);
 
 // rope with a host-built {cos, sin} table [table_len][d/2] (rope.cu).
 int rope_apply_table(wginferDataType_t dtype, void *out, const void *in, const int64_t *pos_ids, const float2 *table,
                      int table_len, int S, int H, int d, cudaStream_t s);
+
+// Fused decode GEMV (decode_gemv.cu). Rows of x: M0 (processed 8 at a time).
+struct DecodeGemvParams {
+    const void *w;       // [N, K]
+    const void *x;       // [M0, K]
+    int M0, M, N, K;     // M is set per launch
+    int groups;          // weight-row pairs this call covers
+    // prologue RMS
+    const void *norm_w;
+    float eps;
+    // epilogue STORE / SWIGLU
+    void *out;           // [M0, ldo]
+    int ldo;
+    const void *bias;    // indexed by weight row, may be null
+    const void *res;     // residual [M0, ldo] (STORE), may be null or alias out
+    int di;              // SWIGLU: gate rows [0, di), up rows [di, 2 di)
+    // epilogue ROPEKV
+    const int64_t *pos;  // [M0]
+    const float2 *table; // [maxseq][dh / 2]
+    void *q_out;         // [M0, nh, dh]
+    void *kc, *vc;       // cache of sequence 0 for this layer
+    size_t seq_stride;   // elements per sequence in kc / vc
+    int nh, nkvh, dh, maxseq, prefill_seq;
+    unsigned long long *err;
+    // weights of the kernels that follow, pulled into L2 while this one runs
+    const void *pf_ptr[2];
+    size_t pf_bytes[2];
+};
+enum { DG_PRO_PLAIN = 0, DG_PRO_RMS = 1, DG_EPI_STORE = 0, DG_EPI_SWIGLU = 1, DG_EPI_ROPEKV = 2 };
+int decode_gemv(wginferDataType_t dtype, const DecodeGemvParams &p, int pro, int epi, cudaStream_t s);
+void decode_gemv_prepare();  // raises shared-memory limits; call outside graph capture
 
 }  // namespace wgb

@@ -3,13 +3,11 @@
 // Dispatch (wgb_linear):
 //  - FAST, bf16, M > kGemvMaxM, aligned: tcgen05 tensor-core GEMM
 //    (linear_tc.cu) with the bias fused in its epilogue.
-//  - FAST, M <= kGemvMaxM per pass: weight-streaming GEMV. A warp owns R
-//    weight rows and a 1/KS slice of K; every lane streams 16-byte weight
-//    vectors (evict-first in L2, since each weight is read once per call)
-//    and applies them to all M input rows held next to it, so W crosses HBM
-//    once for up to 8 rows. Partial sums meet in shared memory and the bias
-//    is added before the single rounding. Roofline: HBM,
-//    (N*K + M*K + M*N + N) * size bytes.
+//  - FAST otherwise: the weight-streaming GEMV of decode_gemv.cu (a warp
+//    owns two weight rows and a slice of K; lanes stream 16-byte weight
+//    vectors evict-first and apply them to up to 8 input rows at once, so W
+//    crosses HBM once per 8 rows; the bias is added before the single
+//    rounding). Roofline: HBM, (N*K + M*K + M*N + N) * size bytes.
 //  - REFERENCE: every output is one sequential f32 chain over k in order,
 //    starting from 0 (+ bias), as src/ops/linear/cpu/linear_cpu.cpp:75-107
 //    (f16/bf16) and :25-72 (f32) compute it; bf16/f16 products are exact in
@@ -37,111 +35,6 @@ __device__ __forceinline__ void store_out(T *out, const T *res, size_t idx, floa
         s = __fadd_rn(ldf(res, idx), r);
     }
     stf(out, idx, s);
-}
-
-template <typename T, int MT, int R, int KS>
-__global__ void __launch_bounds__(256) gemv_kernel(T *out, const T *__restrict__ x,
-                                                   const T *__restrict__ w, const T *__restrict__ bias,
-                                                   const T *res, int M, int N, int K, int ldo) {
-    constexpr int V = Vec16<T>::N;
-    constexpr int GROUPS = 8 / KS;  // row groups per CTA
-    __shared__ float red[8][R][MT];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int rg = warp / KS, ks = warp % KS;
-    const int n0 = (blockIdx.x * GROUPS + rg) * R;
-    const int nvec = K / V;
-    const int per = (nvec + KS - 1) / KS;
-    const int v0 = ks * per, v1 = min(v0 + per, nvec);
-
-    float acc[R][MT];
-#pragma unroll
-    for (int r = 0; r < R; r++)
-#pragma unroll
-        for (int m = 0; m < MT; m++) acc[r][m] = 0.f;
-
-    const T *wrow[R];
-    bool rok[R];
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-        rok[r] = n0 + r < N;
-        wrow[r] = w + (size_t)(rok[r] ? n0 + r : 0) * K;
-    }
-
-    const uint64_t pol = evict_first_policy();
-    int vi = v0 + lane;
-    for (; vi + 32 < v1; vi += 64) {
-        Vec16<T> wv[2][R], xv[2][MT];
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-#pragma unroll
-            for (int r = 0; r < R; r++) wv[u][r].u = ld_stream_v4(wrow[r] + (size_t)(vi + 32 * u) * V, pol);
-#pragma unroll
-            for (int m = 0; m < MT; m++)
-                xv[u][m].u = m < M ? ld_global_nc_v4(x + (size_t)m * K + (size_t)(vi + 32 * u) * V) : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int u = 0; u < 2; u++)
-#pragma unroll
-            for (int e = 0; e < V; e++)
-#pragma unroll
-                for (int r = 0; r < R; r++) {
-                    const float wf = Elem<T>::load(wv[u][r].e[e]);
-#pragma unroll
-                    for (int m = 0; m < MT; m++) acc[r][m] = fmaf(Elem<T>::load(xv[u][m].e[e]), wf, acc[r][m]);
-                }
-    }
-    for (; vi < v1; vi += 32) {
-        Vec16<T> wv[R], xv[MT];
-#pragma unroll
-        for (int r = 0; r < R; r++) wv[r].u = ld_stream_v4(wrow[r] + (size_t)vi * V, pol);
-#pragma unroll
-        for (int m = 0; m < MT; m++)
-            xv[m].u = m < M ? ld_global_nc_v4(x + (size_t)m * K + (size_t)vi * V) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-        for (int e = 0; e < V; e++)
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                const float wf = Elem<T>::load(wv[r].e[e]);
-#pragma unroll
-                for (int m = 0; m < MT; m++) acc[r][m] = fmaf(Elem<T>::load(xv[m].e[e]), wf, acc[r][m]);
-            }
-    }
-#pragma unroll
-    for (int r = 0; r < R; r++)
-#pragma unroll
-        for (int m = 0; m < MT; m++) acc[r][m] = warp_sum(acc[r][m]);
-    if (KS == 1) {
-        if (lane < R * MT) {
-            const int r = lane / MT, m = lane % MT;
-            float s = 0.f;
-#pragma unroll
-            for (int rr = 0; rr < R; rr++)
-#pragma unroll
-                for (int mm = 0; mm < MT; mm++)
-                    if (rr == r && mm == m) s = acc[rr][mm];
-            if (m < M && n0 + r < N) {
-                if (bias) s += ldf(bias, n0 + r);
-                store_out(out, res, (size_t)m * ldo + n0 + r, s);
-            }
-        }
-        return;
-    }
-    if (lane == 0) {
-#pragma unroll
-        for (int r = 0; r < R; r++)
-#pragma unroll
-            for (int m = 0; m < MT; m++) red[warp][r][m] = acc[r][m];
-    }
-    __syncthreads();
-    if (ks == 0 && lane < R * MT) {
-        const int r = lane / MT, m = lane % MT;
-        float s = 0.f;
-        for (int q = 0; q < KS; q++) s += red[warp + q][r][m];
-        if (m < M && n0 + r < N) {
-            if (bias) s += ldf(bias, n0 + r);
-            store_out(out, res, (size_t)m * ldo + n0 + r, s);
-        }
-    }
 }
 
 template <typename T>
@@ -172,7 +65,7 @@ __device__ __forceinline__ float chain_step(float acc, float xv, float wv) {
     return kExactProduct ? fmaf(xv, wv, acc) : __fadd_rn(acc, __fmul_rn(xv, wv));
 }
 
-template <typename T>
+template <typename T, int MT>
 __global__ void __launch_bounds__(kRefRows) gemv_ref_kernel(T *out, const T *__restrict__ x,
                                                             const T *__restrict__ w, const T *__restrict__ bias,
                                                             const T *res, int M, int N, int K) {
@@ -181,12 +74,12 @@ __global__ void __launch_bounds__(kRefRows) gemv_ref_kernel(T *out, const T *__r
     constexpr int KT = 128 / sizeof(T);   // k per tile: 64 (bf16/f16) or 32 (f32)
     constexpr int LDW = KT + V;           // padded row stride: 144 bytes, conflict-free 16-byte reads
     __shared__ __align__(16) T ws[kRefStages][kRefRows * LDW];
-    __shared__ float xs[kRefStages][kRefMT][KT];
+    __shared__ float xs[kRefStages][MT][KT];
     const int tid = threadIdx.x;
     const int n0 = blockIdx.x * kRefRows;
     const int n = n0 + tid;
-    const int m0 = blockIdx.y * kRefMT;
-    const int mt = min(kRefMT, M - m0);
+    const int m0 = blockIdx.y * MT;
+    const int mt = min(MT, M - m0);
     const int ntiles = (K + KT - 1) / KT;
     const bool vec = (K % V) == 0 && ((reinterpret_cast<uintptr_t>(w) & 15) == 0);
 
@@ -209,17 +102,17 @@ __global__ void __launch_bounds__(kRefRows) gemv_ref_kernel(T *out, const T *__r
                 if (nn < N && kk < kl) ws[st][r * LDW + kk] = w[(size_t)nn * K + k0 + kk];
             }
         }
-        for (int c = tid; c < kRefMT * KT; c += kRefRows) {
+        for (int c = tid; c < MT * KT; c += kRefRows) {
             const int m = c / KT, kk = c % KT;
             xs[st][m][kk] = (m < mt && kk < kl) ? ldf(x, (size_t)(m0 + m) * K + k0 + kk) : 0.f;
         }
         __pipeline_commit();
     };
 
-    float acc[kRefMT];
+    float acc[MT];
     const float b = (bias && n < N) ? ldf(bias, n) : 0.f;
 #pragma unroll
-    for (int m = 0; m < kRefMT; m++) acc[m] = __fadd_rn(0.f, b);
+    for (int m = 0; m < MT; m++) acc[m] = __fadd_rn(0.f, b);
 
     for (int t = 0; t < kRefStages - 1; t++) {
         if (t < ntiles) issue(t);
@@ -242,59 +135,23 @@ __global__ void __launch_bounds__(kRefRows) gemv_ref_kernel(T *out, const T *__r
                 for (int e = 0; e < V; e++) {
                     const float wf = Elem<T>::load(wv.e[e]);
 #pragma unroll
-                    for (int m = 0; m < kRefMT; m++) acc[m] = chain_step<kExact>(acc[m], xs[st][m][k8 + e], wf);
+                    for (int m = 0; m < MT; m++) acc[m] = chain_step<kExact>(acc[m], xs[st][m][k8 + e], wf);
                 }
             }
         } else {
             for (int kk = 0; kk < kl; kk++) {
                 const float wf = Elem<T>::load(wr[kk]);
 #pragma unroll
-                for (int m = 0; m < kRefMT; m++) acc[m] = chain_step<kExact>(acc[m], xs[st][m][kk], wf);
+                for (int m = 0; m < MT; m++) acc[m] = chain_step<kExact>(acc[m], xs[st][m][kk], wf);
             }
         }
         __syncthreads();
     }
     if (n < N) {
 #pragma unroll
-        for (int m = 0; m < kRefMT; m++)
+        for (int m = 0; m < MT; m++)
             if (m < mt) store_out(out, res, (size_t)(m0 + m) * N + n, acc[m]);
     }
-}
-
-template <typename T, int MT>
-int launch_gemv_mt(T *out, const T *x, const T *w, const T *bias, const T *res, int M, int N, int K, cudaStream_t s) {
-    constexpr int V = Vec16<T>::N;
-    constexpr int R = 2;
-    const int nvec = K / V;
-    const int iters = (nvec + 31) / 32;
-    int ks = (iters + 3) / 4;
-    ks = ks >= 8 ? 8 : ks >= 4 ? 4 : ks >= 2 ? 2 : 1;
-    const int groups = 8 / ks;
-    const int blocks = (N + groups * R - 1) / (groups * R);
-    switch (ks) {
-    case 1: gemv_kernel<T, MT, R, 1><<<blocks, 256, 0, s>>>(out, x, w, bias, res, M, N, K, N); break;
-    case 2: gemv_kernel<T, MT, R, 2><<<blocks, 256, 0, s>>>(out, x, w, bias, res, M, N, K, N); break;
-    case 4: gemv_kernel<T, MT, R, 4><<<blocks, 256, 0, s>>>(out, x, w, bias, res, M, N, K, N); break;
-    default: gemv_kernel<T, MT, R, 8><<<blocks, 256, 0, s>>>(out, x, w, bias, res, M, N, K, N); break;
-    }
-    return check_launch("linear(gemv)");
-}
-
-template <typename T>
-int launch_gemv(T *out, const T *x, const T *w, const T *bias, const T *res, int M, int N, int K, cudaStream_t s) {
-    for (int m0 = 0; m0 < M; m0 += kGemvMaxM) {
-        const int mm = min(kGemvMaxM, M - m0);
-        T *o = out + (size_t)m0 * N;
-        const T *xx = x + (size_t)m0 * K;
-        const T *rr = res ? res + (size_t)m0 * N : nullptr;
-        int rc;
-        if (mm == 1) rc = launch_gemv_mt<T, 1>(o, xx, w, bias, rr, mm, N, K, s);
-        else if (mm == 2) rc = launch_gemv_mt<T, 2>(o, xx, w, bias, rr, mm, N, K, s);
-        else if (mm <= 4) rc = launch_gemv_mt<T, 4>(o, xx, w, bias, rr, mm, N, K, s);
-        else rc = launch_gemv_mt<T, 8>(o, xx, w, bias, rr, mm, N, K, s);
-        if (rc) return rc;
-    }
-    return WGB_OK;
 }
 
 template <typename T>
@@ -302,15 +159,35 @@ int launch_linear(T *out, const T *x, const T *w, const T *bias, const T *res, s
                   bool ref, cudaStream_t s) {
     constexpr int V = Vec16<T>::N;
     if (ref) {
-        dim3 grid((unsigned)((N + kRefRows - 1) / kRefRows), (unsigned)((M + kRefMT - 1) / kRefMT));
+        // one input row: one chain per thread; otherwise eight chains per thread
+        const int mt = M == 1 ? 1 : kRefMT;
+        dim3 grid((unsigned)((N + kRefRows - 1) / kRefRows), (unsigned)((M + mt - 1) / mt));
         WGB_REQUIRE(grid.y <= 65535, WGB_ERR_INVALID_ARGUMENT, "wgb_linear: M too large");
-        gemv_ref_kernel<T><<<grid, kRefRows, 0, s>>>(out, x, w, bias, res, (int)M, (int)N, (int)K);
+        if (mt == 1) gemv_ref_kernel<T, 1><<<grid, kRefRows, 0, s>>>(out, x, w, bias, res, (int)M, (int)N, (int)K);
+        else gemv_ref_kernel<T, kRefMT><<<grid, kRefRows, 0, s>>>(out, x, w, bias, res, (int)M, (int)N, (int)K);
         return check_launch("linear(reference)");
     }
     const bool vec = (K % V) == 0 && aligned16(x) && aligned16(w);
     if (std::is_same<T, __nv_bfloat16>::value && vec && M > (size_t)kGemvMaxM && linear_tc_supported(M, N, K, out, x, w))
         return linear_tc_bf16(out, x, w, bias, res, (int)M, (int)N, (int)K, s);
-    if (vec) return launch_gemv(out, x, w, bias, res, (int)M, (int)N, (int)K, s);
+    if (vec) {
+        // the weight-streaming GEMV of decode_gemv.cu, plain prologue and store epilogue
+        DecodeGemvParams p{};
+        p.w = w;
+        p.x = x;
+        p.M0 = (int)M;
+        p.N = (int)N;
+        p.K = (int)K;
+        p.groups = (int)((N + 1) / 2);
+        p.out = out;
+        p.ldo = (int)N;
+        p.bias = bias;
+        p.res = res;
+        const wginferDataType_t dt = std::is_same<T, float>::value    ? WGINFER_DTYPE_F32
+                                     : std::is_same<T, __half>::value ? WGINFER_DTYPE_F16
+                                                                      : WGINFER_DTYPE_BF16;
+        return decode_gemv(dt, p, DG_PRO_PLAIN, DG_EPI_STORE, s);
+    }
     const size_t want = (M * N + 7) / 8;
     const int cap = sm_count() * 8;
     gemv_scalar_kernel<T><<<(int)(want < (size_t)cap ? want : cap), 256, 0, s>>>(out, x, w, bias, res, (int)M,

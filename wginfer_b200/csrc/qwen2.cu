@@ -198,8 +198,53 @@ namespace {
 
 int cuda_err(const char *what) { return check_launch(what); }
 
-// One transformer layer over T rows (model.cpp:243-328).
-int run_layer(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t total_len, bool ref) {
+// Per-launch device timing of an eagerly launched decode step
+// (wgb_qwen2_trace_step): an event after every launch on the model stream.
+struct Tracer {
+    bool on = false;
+    cudaStream_t s = nullptr;
+    std::vector<cudaEvent_t> ev;
+    std::vector<const char *> names;
+    void mark(const char *name) {
+        if (!on) return;
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+        cudaStreamIsCapturing(s, &st);
+        if (st == cudaStreamCaptureStatusActive) cudaEventRecordWithFlags(e, s, cudaEventRecordExternal);
+        else cudaEventRecord(e, s);
+        ev.push_back(e);
+        names.push_back(name);
+    }
+};
+thread_local Tracer t_trace;
+#define WGB_TRACE(name) t_trace.mark(name)
+
+// self_attention for one layer: dense causal over the prefill sequence's
+// cache, or batched decode over every row's own cache.
+int attention(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t total_len, bool ref,
+              const void *pf_ptr = nullptr, size_t pf_bytes = 0) {
+    const wgbQwen2Meta &m = M->m;
+    cudaStream_t s = M->stream;
+    const float scale = 1.0f / sqrtf((float)m.dh);
+    if (prefill_seq >= 0) {
+        const char *kb = (const char *)M->layer_k(l) + (size_t)prefill_seq * M->seq_stride * M->es;
+        const char *vb = (const char *)M->layer_v(l) + (size_t)prefill_seq * M->seq_stride * M->es;
+        int prev = wgb_get_numerics();
+        wgb_set_numerics(ref ? WGB_NUMERICS_REFERENCE : WGB_NUMERICS_FAST);
+        int rc = wgb_self_attention_ex(M->att, M->qr, kb, vb, M->dt, T, m.nh, m.nkvh, m.dh, m.dh, total_len, scale,
+                                       M->attn_ws, M->attn_ws_bytes, s);
+        wgb_set_numerics(prev);
+        return rc;
+    }
+    return attn_decode(M->dt, M->att, M->qr, M->layer_k(l), M->layer_v(l), M->seq_stride, M->lens, T, (int)m.nh,
+                       (int)m.nkvh, (int)m.dh, (int)m.maxseq, scale, M->attn_ws, ref, s, pf_ptr, pf_bytes);
+}
+
+// One transformer layer over T rows (model.cpp:243-328), REFERENCE numerics:
+// the reference's op sequence with each op in the reference summation order.
+int run_layer_ref(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t total_len) {
+    const bool ref = true;
     const wgbQwen2Meta &m = M->m;
     cudaStream_t s = M->stream;
     const LayerW &w = M->L[l];
@@ -218,21 +263,7 @@ int run_layer(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t total_l
                                                      M->seq_stride, dev_error_ptr()));
         if ((rc = cuda_err("qkv_post"))) return rc;
     }
-    const float scale = 1.0f / sqrtf((float)m.dh);
-    if (prefill_seq >= 0) {
-        const char *kb = (const char *)M->layer_k(l) + (size_t)prefill_seq * M->seq_stride * M->es;
-        const char *vb = (const char *)M->layer_v(l) + (size_t)prefill_seq * M->seq_stride * M->es;
-        int prev = wgb_get_numerics();
-        wgb_set_numerics(ref ? WGB_NUMERICS_REFERENCE : WGB_NUMERICS_FAST);
-        rc = wgb_self_attention_ex(M->att, M->qr, kb, vb, M->dt, T, m.nh, m.nkvh, m.dh, m.dh, total_len, scale,
-                                   M->attn_ws, M->attn_ws_bytes, s);
-        wgb_set_numerics(prev);
-        if (rc) return rc;
-    } else {
-        if ((rc = attn_decode(M->dt, M->att, M->qr, M->layer_k(l), M->layer_v(l), M->seq_stride, M->lens, T,
-                              (int)m.nh, (int)m.nkvh, (int)m.dh, (int)m.maxseq, scale, M->attn_ws, ref, s)))
-            return rc;
-    }
+    if ((rc = attention(M, l, T, prefill_seq, total_len, ref))) return rc;
     // o_proj with the residual add fused: x = x + o(att)
     if ((rc = linear_forward(M->dt, M->x, M->att, w.o_w, nullptr, M->x, T, hs, (int)(m.nh * m.dh), ref, s))) return rc;
     if ((rc = wgb_rms_norm(M->xn, M->x, w.mlp_norm, M->dt, T, hs, m.epsilon, s))) return rc;
@@ -241,11 +272,140 @@ int run_layer(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t total_l
         const size_t n = (size_t)T * di;
         const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)sm_count() * 8);
         WGB_DISPATCH_FLOAT(M->dt, Tt,
-            if (ref) swiglu_rows_kernel<Tt, true><<<blocks, 256, 0, s>>>((Tt *)M->act, (const Tt *)M->gu, T, di);
-            else swiglu_rows_kernel<Tt, false><<<blocks, 256, 0, s>>>((Tt *)M->act, (const Tt *)M->gu, T, di));
+            swiglu_rows_kernel<Tt, true><<<blocks, 256, 0, s>>>((Tt *)M->act, (const Tt *)M->gu, T, di));
         if ((rc = cuda_err("swiglu_rows"))) return rc;
     }
     return linear_forward(M->dt, M->x, M->act, w.down_w, nullptr, M->x, T, hs, di, ref, s);
+}
+
+// The same layer in FAST numerics: five launches, each chained to the
+// previous one by programmatic dependent launch (decode_gemv.cu).
+int run_layer_fast(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t total_len) {
+    const wgbQwen2Meta &m = M->m;
+    cudaStream_t s = M->stream;
+    const LayerW &w = M->L[l];
+    const int hs = (int)m.hs, di = (int)m.di, half = (int)m.dh / 2;
+    const size_t es = M->es;
+    const size_t qkv_b = M->nq() * m.hs * es, o_b = m.hs * m.nh * m.dh * es, gu_b = 2 * m.di * m.hs * es,
+                 down_b = m.hs * m.di * es;
+    const bool last = l + 1 == m.nlayer;
+    const void *next_qkv = last ? M->out_embed : M->L[l + 1].qkv_w;
+    const size_t next_qkv_b = last ? std::min<size_t>(m.voc * m.hs * es, 32u << 20) : qkv_b;
+    int rc;
+    DecodeGemvParams p{};
+    p.M0 = T;
+    p.pf_ptr[0] = w.o_w;      // each kernel pulls the following weights into L2
+    p.pf_bytes[0] = o_b;
+    p.pf_ptr[1] = w.gu_w;
+    p.pf_bytes[1] = gu_b / 2;
+    p.eps = m.epsilon;
+    p.err = dev_error_ptr();
+    // rms_norm + q/k/v projection + bias + RoPE + K/V cache append
+    p.w = w.qkv_w;
+    p.x = M->x;
+    p.N = (int)M->nq();
+    p.K = hs;
+    p.groups = (int)((m.nh + m.nkvh) * half + m.nkvh * m.dh / 2);
+    p.norm_w = w.attn_norm;
+    p.bias = w.qkv_b;
+    p.pos = M->pos;
+    p.table = M->rope_table;
+    p.q_out = M->qr;
+    p.kc = M->layer_k(l);
+    p.vc = M->layer_v(l);
+    p.seq_stride = M->seq_stride;
+    p.nh = (int)m.nh;
+    p.nkvh = (int)m.nkvh;
+    p.dh = (int)m.dh;
+    p.maxseq = (int)m.maxseq;
+    p.prefill_seq = prefill_seq;
+    if ((rc = decode_gemv(M->dt, p, DG_PRO_RMS, DG_EPI_ROPEKV, s))) return rc;
+    WGB_TRACE("qkv_gemv+rms+rope+kv");
+    if ((rc = attention(M, l, T, prefill_seq, total_len, false, (const char *)w.gu_w + gu_b / 2, gu_b / 2)))
+        return rc;
+    WGB_TRACE("attention");
+    // o_proj + residual
+    DecodeGemvParams o{};
+    o.M0 = T;
+    o.w = w.o_w;
+    o.x = M->att;
+    o.N = hs;
+    o.K = (int)(m.nh * m.dh);
+    o.groups = (hs + 1) / 2;
+    o.out = M->x;
+    o.ldo = hs;
+    o.res = M->x;
+    o.pf_ptr[0] = w.down_w;
+    o.pf_bytes[0] = down_b;
+    if ((rc = decode_gemv(M->dt, o, DG_PRO_PLAIN, DG_EPI_STORE, s))) return rc;
+    WGB_TRACE("o_gemv+residual");
+    // rms_norm + gate/up projection + SwiGLU
+    DecodeGemvParams g{};
+    g.M0 = T;
+    g.w = w.gu_w;
+    g.x = M->x;
+    g.N = 2 * di;
+    g.K = hs;
+    g.groups = di;
+    g.norm_w = w.mlp_norm;
+    g.eps = m.epsilon;
+    g.out = M->act;
+    g.ldo = di;
+    g.di = di;
+    g.pf_ptr[0] = next_qkv;
+    g.pf_bytes[0] = next_qkv_b;
+    if ((rc = decode_gemv(M->dt, g, DG_PRO_RMS, DG_EPI_SWIGLU, s))) return rc;
+    WGB_TRACE("gate_up_gemv+rms+swiglu");
+    // down_proj + residual
+    DecodeGemvParams d{};
+    d.M0 = T;
+    d.w = w.down_w;
+    d.x = M->act;
+    d.N = hs;
+    d.K = di;
+    d.groups = (hs + 1) / 2;
+    d.out = M->x;
+    d.ldo = hs;
+    d.res = M->x;
+    if (!last) {
+        d.pf_ptr[0] = M->L[l + 1].o_w;
+        d.pf_bytes[0] = o_b;
+        d.pf_ptr[1] = M->L[l + 1].gu_w;
+        d.pf_bytes[1] = gu_b / 2;
+    } else {
+        d.pf_ptr[0] = (const char *)M->out_embed + next_qkv_b;
+        d.pf_bytes[0] = std::min<size_t>(m.voc * m.hs * es - next_qkv_b, 32u << 20);
+    }
+    rc = decode_gemv(M->dt, d, DG_PRO_PLAIN, DG_EPI_STORE, s);
+    WGB_TRACE("down_gemv+residual");
+    return rc;
+}
+
+int run_layer(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t total_len, bool ref) {
+    return ref ? run_layer_ref(M, l, T, prefill_seq, total_len) : run_layer_fast(M, l, T, prefill_seq, total_len);
+}
+
+// final rms_norm + lm_head for `rows` rows of x starting at x_row, into logits.
+int lm_head(wgbQwen2Model *M, const void *x_row, int rows, void *logits, bool ref) {
+    const wgbQwen2Meta &m = M->m;
+    cudaStream_t s = M->stream;
+    int rc;
+    if (ref) {
+        if ((rc = wgb_rms_norm(M->xn, x_row, M->out_norm, M->dt, rows, m.hs, m.epsilon, s))) return rc;
+        return linear_forward(M->dt, logits, M->xn, M->out_embed, nullptr, nullptr, rows, (int)m.voc, (int)m.hs, ref, s);
+    }
+    DecodeGemvParams p{};
+    p.M0 = rows;
+    p.w = M->out_embed;
+    p.x = x_row;
+    p.N = (int)m.voc;
+    p.K = (int)m.hs;
+    p.groups = (int)(m.voc + 1) / 2;
+    p.norm_w = M->out_norm;
+    p.eps = m.epsilon;
+    p.out = logits;
+    p.ldo = (int)m.voc;
+    return decode_gemv(M->dt, p, DG_PRO_RMS, DG_EPI_STORE, s);
 }
 
 // Decode step body for sequences [0, B) (captured into a graph).
@@ -254,14 +414,17 @@ int decode_body(wgbQwen2Model *M, int B, bool ref) {
     cudaStream_t s = M->stream;
     int rc;
     decode_begin_kernel<<<(B + 127) / 128, 128, 0, s>>>(M->pos, M->lens, B);
+    WGB_TRACE("decode_begin");
     if ((rc = wgb_embedding(M->x, M->tokens, M->in_embed, M->dt, B, m.hs, m.voc, s))) return rc;
+    WGB_TRACE("embedding");
     for (size_t l = 0; l < m.nlayer; l++)
         if ((rc = run_layer(M, l, B, -1, 0, ref))) return rc;
-    if ((rc = wgb_rms_norm(M->xn, M->x, M->out_norm, M->dt, B, m.hs, m.epsilon, s))) return rc;
-    if ((rc = linear_forward(M->dt, M->logits, M->xn, M->out_embed, nullptr, nullptr, B, (int)m.voc, (int)m.hs, ref, s)))
-        return rc;
+    if ((rc = lm_head(M, M->x, B, M->logits, ref))) return rc;
+    WGB_TRACE("lm_head_gemv+rms");
     if ((rc = wgb_argmax_rows(M->tokens, nullptr, M->logits, M->dt, B, m.voc, s))) return rc;
+    WGB_TRACE("argmax");
     decode_end_kernel<<<(B + 127) / 128, 128, 0, s>>>(M->lens, B, (int)m.maxseq);
+    WGB_TRACE("decode_end");
     return cuda_err("decode_end");
 }
 
@@ -290,9 +453,7 @@ int prefill_impl(wgbQwen2Model *M, int seq, const int64_t *ids_host, size_t n, b
         if (off + T == n) {
             const char *last = (const char *)M->x + (size_t)(T - 1) * m.hs * M->es;
             void *lg = (char *)M->logits + (size_t)seq * m.voc * M->es;
-            if ((rc = wgb_rms_norm(M->xn, last, M->out_norm, M->dt, 1, m.hs, m.epsilon, s))) return rc;
-            if ((rc = linear_forward(M->dt, lg, M->xn, M->out_embed, nullptr, nullptr, 1, (int)m.voc, (int)m.hs, ref, s)))
-                return rc;
+            if ((rc = lm_head(M, last, 1, lg, ref))) return rc;
             if ((rc = wgb_argmax_rows(M->tokens + seq, nullptr, lg, M->dt, 1, m.voc, s))) return rc;
         }
     }
@@ -438,6 +599,7 @@ int wgb_qwen2_create(const wgbQwen2Meta *meta, int device, int max_batch, wgbQwe
         rc = cuda_err("pinned staging");
     if (!rc && cudaStreamSynchronize(M->stream) != cudaSuccess) rc = cuda_err("create sync");
     attn_prepare();
+    decode_gemv_prepare();
     dev_error_ptr();  // resolve the error-word address outside any graph capture
     M->h_lens.assign(max_batch, 0);
     if (rc) {
@@ -580,6 +742,57 @@ int wgb_qwen2_infer(wgbQwen2Model *M, const int64_t *ids, size_t n, int top_k, f
     }
     *next = sample_host(lg, top_k, top_p, temperature);
     return WGB_OK;
+}
+
+int wgb_qwen2_trace_step(wgbQwen2Model *M, int B, int max_launches, float *us, char *names, size_t names_cap,
+                         int *n_launches) {
+    WGB_REQUIRE(M && us && names && n_launches && B >= 1 && B <= M->max_batch, WGB_ERR_INVALID_ARGUMENT,
+                "wgb_qwen2_trace_step: bad argument");
+    cudaSetDevice(M->device);
+    for (int b = 0; b < B; b++)
+        WGB_REQUIRE(M->h_lens[b] < M->m.maxseq, WGB_ERR_OUT_OF_RANGE, "sequence %d is full", b);
+    const bool ref = wgb_get_numerics() == WGB_NUMERICS_REFERENCE;
+    Tracer &t = t_trace;
+    t = Tracer();
+    t.on = true;
+    t.s = M->stream;
+    // capture the step with an event node after every launch, then replay it:
+    // per-launch device times without host launch gaps
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int rc = WGB_OK;
+    if (cudaStreamBeginCapture(M->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) rc = cuda_err("trace capture");
+    if (!rc) {
+        t.mark("start");
+        rc = decode_body(M, B, ref);
+        if (cudaStreamEndCapture(M->stream, &graph) != cudaSuccess && !rc) rc = cuda_err("trace end capture");
+    }
+    t.on = false;
+    if (!rc && cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) rc = cuda_err("trace instantiate");
+    if (!rc && cudaGraphLaunch(exec, M->stream) != cudaSuccess) rc = cuda_err("trace launch");
+    if (cudaStreamSynchronize(M->stream) != cudaSuccess && !rc) rc = cuda_err("trace sync");
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    int n = 0;
+    size_t off = 0;
+    for (size_t i = 1; i < t.ev.size() && n < max_launches; i++, n++) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, t.ev[i - 1], t.ev[i]);
+        us[n] = ms * 1000.f;
+        const size_t len = strlen(t.names[i]);
+        if (off + len + 2 < names_cap) {
+            memcpy(names + off, t.names[i], len);
+            off += len;
+            names[off++] = '\n';
+            names[off] = 0;
+        }
+    }
+    for (auto e : t.ev) cudaEventDestroy(e);
+    t = Tracer();
+    *n_launches = n;
+    if (!rc)
+        for (int b = 0; b < B; b++) M->h_lens[b]++;
+    return rc;
 }
 
 int64_t *wgb_qwen2_token_buffer(wgbQwen2Model *M) { return M ? M->tokens : nullptr; }

@@ -2,6 +2,7 @@
 // error record.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -25,6 +26,14 @@ int check_launch(const char *what) {
 }
 
 int current_numerics() { return t_numerics; }
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("WGB_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
 
 int sm_count() {
     static thread_local int dev = -1, n = kNumSMs;

@@ -102,6 +102,15 @@ class Qwen2:
         _lib.check(self._l.wgb_qwen2_read_tokens(self.h, buf.ctypes.data_as(C.c_void_p), batch), "read_tokens")
         return buf.tolist()
 
+    def trace_step(self, batch: int = 1):
+        """Per-launch device times (us) of one eagerly launched decode step."""
+        us = np.zeros(1024, np.float32)
+        names = C.create_string_buffer(1 << 16)
+        n = C.c_int(0)
+        _lib.check(self._l.wgb_qwen2_trace_step(self.h, batch, 1024, us.ctypes.data_as(C.c_void_p), names,
+                                                1 << 16, C.byref(n)), "trace_step")
+        return list(zip(names.value.decode().split("\n")[:n.value], us[:n.value].tolist()))
+
     def cache_len(self, seq: int = 0) -> int:
         return int(self._l.wgb_qwen2_cache_len(self.h, seq))
 
