@@ -18,6 +18,7 @@
 //    sequences reads and writes a device token buffer and is captured once
 //    into a CUDA graph, so a step costs one graph launch and no host sync.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <algorithm>
 #include <numeric>
@@ -189,6 +190,7 @@ struct wgbQwen2Model {
     // graphs per (batch, numerics)
     std::vector<cudaGraphExec_t> graphs[2];
 
+
     size_t nq() const { return (m.nh + 2 * m.nkvh) * m.dh; }
     void *layer_k(size_t l) const { return (char *)kc + l * max_batch * seq_stride * es; }
     void *layer_v(size_t l) const { return (char *)vc + l * max_batch * seq_stride * es; }
@@ -197,6 +199,8 @@ struct wgbQwen2Model {
 namespace {
 
 int cuda_err(const char *what) { return check_launch(what); }
+
+
 
 // Per-launch device timing of an eagerly launched decode step
 // (wgb_qwen2_trace_step): an event after every launch on the model stream.
@@ -413,6 +417,7 @@ int decode_body(wgbQwen2Model *M, int B, bool ref) {
     const wgbQwen2Meta &m = M->m;
     cudaStream_t s = M->stream;
     int rc;
+
     decode_begin_kernel<<<(B + 127) / 128, 128, 0, s>>>(M->pos, M->lens, B);
     WGB_TRACE("decode_begin");
     if ((rc = wgb_embedding(M->x, M->tokens, M->in_embed, M->dt, B, m.hs, m.voc, s))) return rc;
@@ -573,6 +578,7 @@ int wgb_qwen2_create(const wgbQwen2Meta *meta, int device, int max_batch, wgbQwe
     items.push_back({&M->act, rows * m.di * es});
     items.push_back({&M->logits, (size_t)max_batch * m.voc * es});
     items.push_back({&M->attn_ws, M->attn_ws_bytes});
+
     size_t total = 0;
     for (auto &it : items) total += align256(it.bytes);
     if (cudaMalloc((void **)&M->arena, total) != cudaSuccess) {
@@ -600,6 +606,7 @@ int wgb_qwen2_create(const wgbQwen2Meta *meta, int device, int max_batch, wgbQwe
     if (!rc && cudaStreamSynchronize(M->stream) != cudaSuccess) rc = cuda_err("create sync");
     attn_prepare();
     decode_gemv_prepare();
+
     dev_error_ptr();  // resolve the error-word address outside any graph capture
     M->h_lens.assign(max_batch, 0);
     if (rc) {
