@@ -11,26 +11,14 @@ namespace wgb {
 
 enum Epi { EPI_STORE = DG_EPI_STORE, EPI_SWIGLU = DG_EPI_SWIGLU, EPI_ROPEKV = DG_EPI_ROPEKV };
 
+// Weight row pair g is rows (2g, 2g + 1) for every epilogue: the model stores
+// q/k rows with rotation partners (j, j + dh/2) of a head next to each other
+// and gate/up rows interleaved (qwen2.cu, set_weight), so a pair is always
+// two adjacent rows and a block of pairs is one contiguous byte range.
 template <int EPI>
 __device__ __forceinline__ void row_map(const DecodeGemvParams &p, int g, int &r0, int &r1) {
-    if (EPI == EPI_SWIGLU) {
-        r0 = g;
-        r1 = p.di + g;
-    } else if (EPI == EPI_ROPEKV) {
-        const int half = p.dh >> 1;
-        const int P = (p.nh + p.nkvh) * half;
-        if (g < P) {
-            const int h = g / half, j = g - h * half;
-            r0 = h * p.dh + j;
-            r1 = r0 + half;
-        } else {
-            r0 = (p.nh + p.nkvh) * p.dh + 2 * (g - P);
-            r1 = r0 + 1;
-        }
-    } else {
-        r0 = 2 * g;
-        r1 = 2 * g + 1;
-    }
+    r0 = 2 * g;
+    r1 = 2 * g + 1;
 }
 
 template <typename T, int EPI>

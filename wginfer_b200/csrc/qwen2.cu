@@ -35,9 +35,9 @@ namespace {
 size_t dsize(int dt) { return dt == WGINFER_DTYPE_F32 ? 4 : 2; }
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-// qkv rows [T, (nh + 2 nkvh) * dh] -> q_rope [T, nh, dh] and, for the k/v
-// heads, the cache of sequence seq(t) at position pos[t]. One thread per
-// rotation pair (j, j + dh/2) per head.
+// qkv rows [T, (nh + 2 nkvh) * dh] (q/k columns pair-interleaved: column 2i,
+// 2i+1 = rotation pair i) -> q_rope [T, nh, dh] and, for the k/v heads, the
+// cache of sequence seq(t) at position pos[t]. One thread per rotation pair.
 template <typename T>
 __global__ void __launch_bounds__(128) qkv_post_kernel(const T *__restrict__ qkv, T *__restrict__ q_out, T *kcache,
                                                        T *vcache, const int64_t *__restrict__ pos,
@@ -61,8 +61,8 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(const T *__restrict__ qkv
         if (idx < (nh + nkvh) * half) {
             const int h = idx / half, j = idx - h * half;  // h < nh: q head; else k head h - nh
             const float2 cs = table[(size_t)p * half + j];
-            const T *src = row + (size_t)h * dh;
-            const float a = ldf(src, j), b = ldf(src, j + half);
+            // rotation partners sit side by side (pair-interleaved q/k rows)
+            const float a = ldf(row, 2 * (size_t)idx), b = ldf(row, 2 * (size_t)idx + 1);
             const float o0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
             const float o1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
             T *dst = h < nh ? q_out + ((size_t)t * nh + h) * dh : kc + (size_t)(h - nh) * dh;
@@ -81,10 +81,29 @@ __global__ void __launch_bounds__(256) swiglu_rows_kernel(T *__restrict__ act, c
                                                           int di) {
     const size_t n = (size_t)T_rows * di;
     for (size_t i = (size_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (size_t)gridDim.x * 256) {
-        const size_t t = i / di, j = i - t * di;
-        const float g = ldf(gu, t * 2 * di + j), u = ldf(gu, t * 2 * di + di + j);
+        const size_t t = i / di, j = i - t * di;  // gate and up rows are interleaved
+        const float g = ldf(gu, t * 2 * di + 2 * j), u = ldf(gu, t * 2 * di + 2 * j + 1);
         const float e = kRef ? exp_cr(-g) : expf(-g);
         stf(act, i, __fdiv_rn(__fmul_rn(u, g), __fadd_rn(1.0f, e)));
+    }
+}
+
+// dst row map(r) = src row r for r < nrows; map: kind 0 = rotation-pair
+// interleave of heads of dh rows (row h*dh + c -> h*dh + 2*(c % half) + c / half),
+// kind 1 = stride 2 from `first` (row r -> 2 r + first).
+__global__ void permute_rows_kernel(char *dst, const char *src, int nrows, size_t row_bytes, int kind, int dh,
+                                    int first) {
+    for (int r = blockIdx.x; r < nrows; r += gridDim.x) {
+        int d;
+        if (kind == 0) {
+            const int h = r / dh, c = r - h * dh, half = dh / 2;
+            d = h * dh + 2 * (c % half) + c / half;
+        } else {
+            d = 2 * r + first;
+        }
+        const char *s = src + (size_t)r * row_bytes;
+        char *o = dst + (size_t)d * row_bytes;
+        for (size_t i = threadIdx.x; i < row_bytes; i += blockDim.x) o[i] = s[i];
     }
 }
 
@@ -637,7 +656,8 @@ int wgb_qwen2_set_weight(wgbQwen2Model *M, const char *name, int layer, const vo
     const size_t es = M->es;
     std::string n(name);
     void *dst = nullptr;
-    size_t want = 0;
+    size_t want = 0, row_bytes = 0, nrows = 0;
+    int kind = -1, first = 0;
     if (layer < 0) {
         if (n == "in_embed") dst = M->in_embed, want = m.voc * m.hs * es;
         else if (n == "out_embed") dst = M->out_embed, want = m.voc * m.hs * es;
@@ -646,27 +666,52 @@ int wgb_qwen2_set_weight(wgbQwen2Model *M, const char *name, int layer, const vo
         WGB_REQUIRE((size_t)layer < m.nlayer, WGB_ERR_OUT_OF_RANGE, "layer %d out of range", layer);
         LayerW &w = M->L[layer];
         const size_t qn = m.nh * m.dh, kn = m.nkvh * m.dh;
+        // q/k rows are stored rotation-pair interleaved, gate/up rows
+        // interleaved (see decode_common.cuh); `kind` selects the row map
         if (n == "attn_norm_w") dst = w.attn_norm, want = m.hs * es;
-        else if (n == "attn_q_w") dst = w.qkv_w, want = qn * m.hs * es;
-        else if (n == "attn_k_w") dst = (char *)w.qkv_w + qn * m.hs * es, want = kn * m.hs * es;
+        else if (n == "attn_q_w") dst = w.qkv_w, want = qn * m.hs * es, kind = 0, row_bytes = m.hs * es, nrows = qn;
+        else if (n == "attn_k_w")
+            dst = (char *)w.qkv_w + qn * m.hs * es, want = kn * m.hs * es, kind = 0, row_bytes = m.hs * es, nrows = kn;
         else if (n == "attn_v_w") dst = (char *)w.qkv_w + (qn + kn) * m.hs * es, want = kn * m.hs * es;
-        else if (n == "attn_q_b") dst = w.qkv_b, want = qn * es;
-        else if (n == "attn_k_b") dst = (char *)w.qkv_b + qn * es, want = kn * es;
+        else if (n == "attn_q_b") dst = w.qkv_b, want = qn * es, kind = 0, row_bytes = es, nrows = qn;
+        else if (n == "attn_k_b") dst = (char *)w.qkv_b + qn * es, want = kn * es, kind = 0, row_bytes = es, nrows = kn;
         else if (n == "attn_v_b") dst = (char *)w.qkv_b + (qn + kn) * es, want = kn * es;
         else if (n == "attn_o_w") dst = w.o_w, want = m.hs * qn * es;
         else if (n == "mlp_norm_w") dst = w.mlp_norm, want = m.hs * es;
-        else if (n == "mlp_gate_w") dst = w.gu_w, want = m.di * m.hs * es;
-        else if (n == "mlp_up_w") dst = (char *)w.gu_w + m.di * m.hs * es, want = m.di * m.hs * es;
+        else if (n == "mlp_gate_w") dst = w.gu_w, want = m.di * m.hs * es, kind = 1, first = 0, row_bytes = m.hs * es, nrows = m.di;
+        else if (n == "mlp_up_w") dst = w.gu_w, want = m.di * m.hs * es, kind = 1, first = 1, row_bytes = m.hs * es, nrows = m.di;
         else if (n == "mlp_down_w") dst = w.down_w, want = m.hs * m.di * es;
     }
     WGB_REQUIRE(dst != nullptr, WGB_ERR_INVALID_ARGUMENT, "unknown Qwen2 weight: %s", name);
     WGB_REQUIRE(bytes == want, WGB_ERR_INVALID_ARGUMENT, "weight %s: %zu bytes given, %zu expected", name, bytes, want);
     cudaSetDevice(M->device);
-    if (cudaMemcpyAsync(dst, src, bytes, on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, M->stream) !=
-            cudaSuccess ||
-        cudaStreamSynchronize(M->stream) != cudaSuccess)
-        return cuda_err("wgb_qwen2_set_weight");
-    return WGB_OK;
+    if (kind < 0) {
+        if (cudaMemcpyAsync(dst, src, bytes, on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, M->stream) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(M->stream) != cudaSuccess)
+            return cuda_err("wgb_qwen2_set_weight");
+        return WGB_OK;
+    }
+    // rows are scattered into the interleaved layout (a one-time copy)
+    const void *dsrc = src;
+    void *tmp = nullptr;
+    if (on_host) {
+        if (cudaMalloc(&tmp, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            return set_error(WGB_ERR_NO_MEMORY, "wgb_qwen2_set_weight: staging %zu bytes", bytes);
+        }
+        if (cudaMemcpyAsync(tmp, src, bytes, cudaMemcpyHostToDevice, M->stream) != cudaSuccess) {
+            cudaFree(tmp);
+            return cuda_err("wgb_qwen2_set_weight H2D");
+        }
+        dsrc = tmp;
+    }
+    permute_rows_kernel<<<(unsigned)std::min<size_t>(nrows, 4096), 128, 0, M->stream>>>(
+        (char *)dst, (const char *)dsrc, (int)nrows, row_bytes, kind, (int)m.dh, first);
+    int rc = cuda_err("permute_rows");
+    if (cudaStreamSynchronize(M->stream) != cudaSuccess && !rc) rc = cuda_err("wgb_qwen2_set_weight");
+    if (tmp) cudaFree(tmp);
+    return rc;
 }
 
 int wgb_qwen2_reset_cache(wgbQwen2Model *M) {
