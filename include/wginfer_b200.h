@@ -61,6 +61,10 @@ __export int wgb_get_numerics(void);
 /* Device-side error record: kernels that find bad data (an embedding index
  * outside [0, vocab)) record the first offending value here instead of
  * faulting. Reads and clears it; *code is 0 when nothing was recorded.
+ * Codes: 1 embedding index out of range (value = the index); 2 rope
+ * position outside its table; 3 decode position outside the KV cache
+ * (value = the position); 6 a tensor-core
+ * linear tile whose copy pipeline stalled (value = the tile's block index).
  * Synchronises `stream`. */
 __export int wgb_device_error(int64_t *code, int64_t *value, wginferStream_t stream);
 

@@ -174,6 +174,42 @@ def test_linear_unaligned_and_ragged(oracle, cuda, mode):
         np.testing.assert_allclose(as_f32(got), as_f32(want), rtol=2e-2, atol=1e-2)
 
 
+# More than 8 bf16 rows take the tcgen05 GEMM (TMA-fed shared-memory ring,
+# f32 accumulator in tensor memory). Shapes cover ragged M (tile of 16..128
+# rows), N not a multiple of the 128-row weight tile, odd N, K below one
+# 64-wide slice and K not a multiple of it (zero-filled by the copy engine).
+TC_SHAPES = [(9, 128, 64), (20, 256, 1536), (64, 1536, 1536), (64, 17920, 1536), (100, 1536, 8960),
+             (512, 2048, 1536), (200, 37, 104), (33, 300, 24), (1000, 96, 200)]
+
+
+@pytest.mark.parametrize("M,N,K", TC_SHAPES)
+@pytest.mark.parametrize("bias", [True, False])
+def test_linear_tensor_core_vs_torch(cuda, M, N, K, bias):
+    x = _bf16((M, K), M * 7 + K)
+    w = _bf16((N, K), N * 3 + K, 0.02)
+    b = _bf16((N,), N, 0.5) if bias else None
+    out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    with numerics("fast"):
+        ops.linear(out, x, w, b)
+    ref = x.float() @ w.float().T
+    if bias:
+        ref = ref + b.float()
+    torch.testing.assert_close(out.float(), ref.to(torch.bfloat16).float(), rtol=2e-2, atol=1e-2)
+    assert ops.device_error() == (0, 0)
+
+
+def test_linear_tensor_core_vs_oracle(oracle, cuda):
+    M, N, K = 40, 260, 1536
+    x, w, b = _bf16((M, K), 11), _bf16((N, K), 12, 0.02), _bf16((N,), 13, 0.02)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    with numerics("fast"):
+        ops.linear(out, x, w, b)
+    h = lambda t: t.cpu().view(torch.int16).numpy().view(np.uint16)
+    want = np.zeros((M, N), np.uint16)
+    oracle.linear(want, h(x), h(w), h(b), 15)
+    np.testing.assert_allclose(as_f32(h(out)), as_f32(want), rtol=2e-2, atol=1e-2)
+
+
 def test_attention_workspace_contract(cuda):
     """FAST needs no workspace (the cluster folds its key slices in shared
     memory); REFERENCE keeps one score per key in the workspace once the cache

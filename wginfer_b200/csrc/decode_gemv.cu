@@ -261,6 +261,20 @@ int launch_mt(const DecodeGemvParams &p, cudaStream_t s) {
 
 template <typename T>
 int dispatch(const DecodeGemvParams &p0, int pro, int epi, cudaStream_t s) {
+    // more than 8 rows of bf16: one tensor-core GEMM over all rows (the RMS
+    // prologue first materialised into p0.xn)
+    if (std::is_same<T, __nv_bfloat16>::value && p0.M0 > kMaxMT && (pro == PRO_PLAIN || p0.xn)) {
+        DecodeGemvParams p = p0;
+        p.M = p0.M0;
+        if (pro == PRO_RMS) p.x = p0.xn;
+        if (tc_gemm_ok(p)) {
+            if (pro == PRO_RMS) {
+                const int rc = wgb_rms_norm(p0.xn, p0.x, p0.norm_w, WGINFER_DTYPE_BF16, p0.M0, p0.K, p0.eps, s);
+                if (rc) return rc;
+            }
+            return tc_gemm(p, epi, s);
+        }
+    }
     // chunks of up to 8 input rows; each chunk re-reads the weights
     for (int m0 = 0; m0 < p0.M0; m0 += kMaxMT) {
         DecodeGemvParams p = p0;
@@ -308,6 +322,7 @@ template <typename T> void attrs_all() {
 }  // namespace
 
 void decode_gemv_prepare() {
+    tc_gemm_prepare();
     attrs_all<float>();
     attrs_all<__nv_bfloat16>();
     attrs_all<__half>();

@@ -57,9 +57,19 @@ struct DecodeGemvParams {
     // weights of the kernels that follow, pulled into L2 while this one runs
     const void *pf_ptr[2];
     size_t pf_bytes[2];
+    // [M0, K] scratch for the normalised rows when more than 8 rows take the
+    // tensor-core path with the RMS prologue (may be null: GEMV chunks then)
+    void *xn;
 };
 enum { DG_PRO_PLAIN = 0, DG_PRO_RMS = 1, DG_EPI_STORE = 0, DG_EPI_SWIGLU = 1, DG_EPI_ROPEKV = 2 };
 int decode_gemv(wginferDataType_t dtype, const DecodeGemvParams &p, int pro, int epi, cudaStream_t s);
 void decode_gemv_prepare();  // raises shared-memory limits; call outside graph capture
+
+// The same projections and epilogues on the tensor cores, for bf16 with
+// more than 8 rows (linear_tc.cu). Rows index x, out, pos, q_out and, when
+// prefill_seq < 0, the sequence; the prologue must already be applied.
+bool tc_gemm_ok(const DecodeGemvParams &p);
+int tc_gemm(const DecodeGemvParams &p, int epi, cudaStream_t s);
+void tc_gemm_prepare();
 
 }  // namespace wgb

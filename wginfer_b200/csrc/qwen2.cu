@@ -342,6 +342,7 @@ int run_layer_fast(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t to
     p.dh = (int)m.dh;
     p.maxseq = (int)m.maxseq;
     p.prefill_seq = prefill_seq;
+    p.xn = M->xn;
     if ((rc = decode_gemv(M->dt, p, DG_PRO_RMS, DG_EPI_ROPEKV, s))) return rc;
     WGB_TRACE("qkv_gemv+rms+rope+kv");
     if ((rc = attention(M, l, T, prefill_seq, total_len, false, (const char *)w.gu_w + gu_b / 2, gu_b / 2)))
@@ -377,6 +378,7 @@ int run_layer_fast(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t to
     g.di = di;
     g.pf_ptr[0] = next_qkv;
     g.pf_bytes[0] = next_qkv_b;
+    g.xn = M->xn;
     if ((rc = decode_gemv(M->dt, g, DG_PRO_RMS, DG_EPI_SWIGLU, s))) return rc;
     WGB_TRACE("gate_up_gemv+rms+swiglu");
     // down_proj + residual
@@ -428,6 +430,7 @@ int lm_head(wgbQwen2Model *M, const void *x_row, int rows, void *logits, bool re
     p.eps = m.epsilon;
     p.out = logits;
     p.ldo = (int)m.voc;
+    p.xn = M->xn;
     return decode_gemv(M->dt, p, DG_PRO_RMS, DG_EPI_STORE, s);
 }
 
