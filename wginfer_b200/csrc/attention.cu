@@ -319,23 +319,34 @@ __global__ void __launch_bounds__(kThreads) attn_fast_kernel(const T *__restrict
 }
 
 // ---- FAST, one head per warp (decode and short query blocks) ---------------
-// Lane j of a warp owns key j of a 32-key chunk and computes its whole dot
-// product from registers (the K row is one coalesced 256-byte read per lane
-// pair of 16-byte vectors), so the score phase has no shared-memory traffic
-// and no block barrier. The warp then folds the chunk into its running
-// (max, sum, output) with shuffles, and for P.V each lane owns DH/32 output
-// columns: V rows are read coalesced across the warp, the weight of key j
-// is broadcast by shuffle. Warps of a CTA take interleaved chunks of the
-// CTA's key slice; the 8 warps, then the cluster's CTAs, are folded in
-// shared memory (the cluster's slices are pushed into CTA 0).
+// Lane j of a warp owns key j of a 32-key chunk: its K row (DH elements) is
+// loaded into registers and the dot product runs from registers, so the
+// score phase has no shared-memory traffic and no block barrier. The same
+// lane copies its V row into the warp's shared-memory buffer with cp.async,
+// so K and V of a chunk arrive in one round trip. The warp folds the chunk
+// into its running (max, sum, output) with shuffles; for P.V each lane owns
+// DH/32 output columns and reads the V rows from shared memory. Warps of a
+// CTA take interleaved chunks of the CTA's key slice; the 8 warps, then the
+// cluster's CTAs, are folded in shared memory (pushed into CTA 0).
+//
+// Over a KV cache (kPre) every row but the newest was written by an earlier
+// step, so a warp's first chunk (K into registers, V into shared memory) is
+// requested before griddepcontrol.wait; the newest row follows the wait.
 constexpr int kWarpKeys = 32;
+
+template <class Src> struct IsKvCache { static constexpr bool value = false; };
+template <typename T> struct IsKvCache<KvCache<T>> { static constexpr bool value = true; };
+
+template <typename T, int DH> constexpr size_t warp_attn_smem() { return (size_t)8 * kWarpKeys * DH * sizeof(T); }
 
 template <typename T, int DH, class Src>
 __global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict__ q, Src src, T *__restrict__ out, AttnShape sh,
                                                              const void *pf_ptr, size_t pf_bytes) {
+    constexpr bool kPre = IsKvCache<Src>::value;
     constexpr int V = 16 / sizeof(T);        // elements per 16-byte vector
     constexpr int NV = DH / V;                // vectors per row
     constexpr int CPL = DH / 32;              // output columns per lane
+    extern __shared__ __align__(16) unsigned char vsm[];  // [8 warps][32 keys][DH] V rows
     __shared__ __align__(16) float qs[DH];
     __shared__ float wm[8], wl[8];
     __shared__ __align__(16) float wo[8][DH];
@@ -357,20 +368,30 @@ __global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict
     const int c0 = rank * per, c1 = min(c0 + per, chunks);
     const size_t kst = (size_t)sh.nkvh * DH;
     const T *kb = k + (size_t)kvh * DH, *vb = v + (size_t)kvh * DH;
-    // Older cache rows are not touched by the previous kernel (it appends
-    // one row): start pulling this CTA's slice into L2 before waiting.
-    if (threadIdx.x == 0 && c0 < c1) {
-        const int r0 = c0 * kWarpKeys, r1 = min(c1 * kWarpKeys, nvis) - 1;  // rows [r0, r1) predate this step
-        if (r1 > r0) {
-            const uint32_t bytes = (uint32_t)((size_t)(r1 - r0) * kst * sizeof(T));
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(k + (size_t)r0 * kst), "r"(bytes) : "memory");
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(v + (size_t)r0 * kst), "r"(bytes) : "memory");
+    T *vs = reinterpret_cast<T *>(vsm) + (size_t)warp * kWarpKeys * DH;  // this warp's V rows
+    const int newest = kPre ? nvis - 1 : -1;  // written by the previous kernel
+
+    Vec16<T> kv[NV];
+    // lane's key j of chunk ch: K row into registers, V row into shared memory
+    auto fetch = [&](int ch) {
+        const int j = ch * kWarpKeys + lane;
+        if (j < nvis) {
+            const uint4 *kr = reinterpret_cast<const uint4 *>(kb + (size_t)j * kst);
+#pragma unroll
+            for (int u = 0; u < NV; u++) kv[u].u = kr[u];
+#pragma unroll
+            for (int u = 0; u < NV; u++)
+                __pipeline_memcpy_async(vs + (size_t)lane * DH + u * V, vb + (size_t)j * kst + u * V, 16);
         }
-    }
+        __pipeline_commit();
+    };
+    const int first = c0 + warp;
+    if (kPre && first < c1 && first * kWarpKeys + lane != newest) fetch(first);
     if (threadIdx.x == 32)  // the next kernel's weights stream into L2 meanwhile
         l2_prefetch_share(pf_ptr, pf_bytes, blockIdx.x + gridDim.x * blockIdx.y, gridDim.x * gridDim.y);
     pdl_trigger();
     pdl_wait();  // q and the newest cache row are written by the previous kernel
+    if (first < c1 && (!kPre || first * kWarpKeys + lane == newest)) fetch(first);
     for (int c = threadIdx.x; c < DH; c += kThreads) qs[c] = ldf(q, ((size_t)i * sh.nh + h) * DH + c);
     __syncthreads();
 
@@ -379,20 +400,20 @@ __global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict
 #pragma unroll
     for (int c = 0; c < CPL; c++) o[c] = 0.f;
 
-    for (int ch = c0 + warp; ch < c1; ch += 8) {
+    for (int ch = first; ch < c1; ch += 8) {
+        if (ch != first) fetch(ch);
         const int j = ch * kWarpKeys + lane;
         const bool ok = j < nvis;
         float sc = -FLT_MAX;
         if (ok) {
-            const uint4 *kr = reinterpret_cast<const uint4 *>(kb + (size_t)j * kst);
-            Vec16<T> kv[NV];
-#pragma unroll
-            for (int u = 0; u < NV; u++) kv[u].u = kr[u];
-            float dot = 0.f;
+            // four independent chains: the dot is latency-bound, not FMA-bound
+            float d4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int u = 0; u < NV; u++)
 #pragma unroll
-                for (int e = 0; e < V; e++) dot = fmaf(qs[u * V + e], Elem<T>::load(kv[u].e[e]), dot);
+                for (int e = 0; e < V; e++)
+                    d4[(u * V + e) & 3] = fmaf(qs[u * V + e], Elem<T>::load(kv[u].e[e]), d4[(u * V + e) & 3]);
+            const float dot = (d4[0] + d4[1]) + (d4[2] + d4[3]);
             sc = uniform ? 0.f : sh.scale * dot;
         }
         const float mnew = fmaxf(m, warp_max(sc));
@@ -403,11 +424,13 @@ __global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict
 #pragma unroll
         for (int c = 0; c < CPL; c++) o[c] *= corr;
         const int nk = min(kWarpKeys, nvis - ch * kWarpKeys);
-        const T *vr = vb + (size_t)(ch * kWarpKeys) * kst + lane * CPL;
+        __pipeline_wait_prior(0);
+        __syncwarp();
+        const T *vr = vs + lane * CPL;
 #pragma unroll 8
         for (int jj = 0; jj < nk; jj++) {
             const float pj = __shfl_sync(0xffffffffu, p, jj);
-            const T *vv = vr + (size_t)jj * kst;
+            const T *vv = vr + (size_t)jj * DH;
             T vl[CPL];
             if constexpr (CPL * sizeof(T) == 16) {
                 *reinterpret_cast<uint4 *>(vl) = *reinterpret_cast<const uint4 *>(vv);
@@ -422,6 +445,7 @@ __global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict
 #pragma unroll
             for (int c = 0; c < CPL; c++) o[c] = fmaf(pj, Elem<T>::load(vl[c]), o[c]);
         }
+        __syncwarp();  // the warp's V buffer is refilled by the next chunk
     }
     // fold the 8 warps
     if (lane == 0) {
@@ -475,7 +499,7 @@ int launch_warp_attn(T *out, const T *q, Src src, const AttnShape &sh, cudaStrea
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ns, (unsigned)(sh.S * sh.nh), 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = warp_attn_smem<T, DH>();
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -638,6 +662,10 @@ template <typename T, class Src> void set_attrs() {
     cudaFuncSetAttribute(attn_ref_kernel<T, Src, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     cudaFuncSetAttribute(attn_fast_kernel<T, Src, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaFuncSetAttribute(attn_fast_kernel<T, Src, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(attn_warp_kernel<T, 128, Src>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)warp_attn_smem<T, 128>());
+    cudaFuncSetAttribute(attn_warp_kernel<T, 64, Src>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)warp_attn_smem<T, 64>());
 }
 
 void init_attrs_once() {

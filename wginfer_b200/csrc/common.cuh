@@ -21,7 +21,11 @@ template <> struct Elem<float> {
     static __device__ __forceinline__ float store(float v) { return v; }
 };
 template <> struct Elem<__nv_bfloat16> {
-    static __device__ __forceinline__ float load(__nv_bfloat16 v) { return __bfloat162float(v); }
+    // bf16 -> f32 is exact: the 16 bits become the high half of the f32
+    // (an integer shift, kept off the conversion pipe)
+    static __device__ __forceinline__ float load(__nv_bfloat16 v) {
+        return __uint_as_float((uint32_t)__bfloat16_as_ushort(v) << 16);
+    }
     static __device__ __forceinline__ __nv_bfloat16 store(float v) { return __float2bfloat16_rn(v); }
 };
 template <> struct Elem<__half> {

@@ -18,7 +18,7 @@
 // Each warp owns two weight rows at a time (chosen by the epilogue's row map)
 // and a 1/KS slice of K; lanes stream 16-byte weight vectors with an L2
 // evict-first policy, several vectors in flight per lane. The grid is
-// persistent (4 CTAs per SM) so the prologue runs once per CTA, and each CTA
+// persistent (every CTA resident at once) so the prologue runs once per CTA, and each CTA
 // prefetches its next block of rows into L2 while it works on the current one.
 //
 // Launch: programmatic dependent launch. A CTA first prefetches its weight
@@ -27,6 +27,8 @@
 // (griddepcontrol.wait); it allows the next kernel to launch at once
 // (griddepcontrol.launch_dependents), so launches and weight fetches overlap
 // the previous kernel's tail.
+#include <atomic>
+
 #include "common.cuh"
 #include "decode_common.cuh"
 #include "kernels.h"
@@ -37,7 +39,7 @@ namespace {
 constexpr int kRows = 2;       // weight rows per warp
 constexpr int kMaxMT = 8;      // input rows per launch
 constexpr int kVPL = 6;        // 16-byte vectors in flight per row per lane
-constexpr int kCtasPerSM = 4;  // persistent grid: 32 resident warps per SM
+constexpr int kCtasPerSM = 4;  // persistent grid: at most 32 resident warps per SM
 
 enum Pro { PRO_PLAIN = DG_PRO_PLAIN, PRO_RMS = DG_PRO_RMS };
 
@@ -46,7 +48,7 @@ __device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
 }
 
 template <typename T, int MT, int KS, int PRO, int EPI>
-__global__ void __launch_bounds__(256) decode_gemv_kernel(DecodeGemvParams p) {
+__global__ void __launch_bounds__(256, (MT <= 2 ? 3 : 2)) decode_gemv_kernel(DecodeGemvParams p) {
     constexpr int V = Vec16<T>::N;
     constexpr int GROUPS = 8 / KS;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -110,15 +112,33 @@ __global__ void __launch_bounds__(256) decode_gemv_kernel(DecodeGemvParams p) {
     pdl_wait();
     const T *x = reinterpret_cast<const T *>(p.x);
     if (PRO == PRO_RMS) {
-        // every (persistent) CTA normalises the few input rows once
-        for (int m = 0; m < M; m++) {
-            float ss = 0.f;
-            for (int i = threadIdx.x; i < K; i += 256) {
-                const float f = ldf(x, (size_t)m * K + i);
-                ss = fmaf(f, f, ss);
+        // every (persistent) CTA normalises the few input rows once: one
+        // round trip of 16-byte loads (x rows and the norm weight together),
+        // raw rows parked in shared memory, a block reduction, then the
+        // scaling pass over shared memory
+        const T *nw = reinterpret_cast<const T *>(p.norm_w);
+        float ss[MT];
+#pragma unroll
+        for (int m = 0; m < MT; m++) ss[m] = 0.f;
+        for (int vi = threadIdx.x; vi < nvec; vi += 256) {
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                if (m < M) {
+                    Vec16<T> xv;
+                    xv.u = *reinterpret_cast<const uint4 *>(x + (size_t)m * K + (size_t)vi * V);
+                    *reinterpret_cast<uint4 *>(xs + (size_t)m * K + (size_t)vi * V) = xv.u;
+#pragma unroll
+                    for (int e = 0; e < V; e++) {
+                        const float f = Elem<T>::load(xv.e[e]);
+                        ss[m] = fmaf(f, f, ss[m]);
+                    }
+                }
             }
-            ss = warp_sum(ss);
-            if (lane == 0) s_part[warp][m] = ss;
+        }
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            const float t = warp_sum(ss[m]);
+            if (lane == 0) s_part[warp][m] = t;
         }
         __syncthreads();
         if (threadIdx.x < MT) {
@@ -128,10 +148,23 @@ __global__ void __launch_bounds__(256) decode_gemv_kernel(DecodeGemvParams p) {
             s_scale[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
         }
         __syncthreads();
-        const T *nw = reinterpret_cast<const T *>(p.norm_w);
-        for (int idx = threadIdx.x; idx < M * K; idx += 256) {
-            const int m = idx / K, i = idx - m * K;
-            xs[idx] = Elem<T>::store(__fmul_rn(__fmul_rn(ldf(x, idx), ldf(nw, i)), s_scale[m]));
+        for (int vi = threadIdx.x; vi < nvec; vi += 256) {
+            Vec16<T> wv;
+            wv.u = ld_global_nc_v4(nw + (size_t)vi * V);
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                if (m < M) {
+                    Vec16<T> xv;
+                    uint4 *q = reinterpret_cast<uint4 *>(xs + (size_t)m * K + (size_t)vi * V);
+                    xv.u = *q;
+                    const float sc = s_scale[m];
+#pragma unroll
+                    for (int e = 0; e < V; e++)
+                        xv.e[e] = Elem<T>::store(
+                            __fmul_rn(__fmul_rn(Elem<T>::load(xv.e[e]), Elem<T>::load(wv.e[e])), sc));
+                    *q = xv.u;
+                }
+            }
         }
         __syncthreads();
         x = xs;
@@ -212,13 +245,41 @@ __global__ void __launch_bounds__(256) decode_gemv_kernel(DecodeGemvParams p) {
     }
 }
 
+// Resident CTAs of 256 threads per SM for one kernel variant with `smem`
+// dynamic shared memory, cached per device and variant (the answer depends
+// only on the kernel's resources); at least 1.
+template <typename T, int MT, int KS, int PRO, int EPI>
+int resident_ctas(size_t smem) {
+    static std::atomic<unsigned long long> cache[64];  // [device] -> (smem + 1) << 8 | ctas
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long key = (unsigned long long)(smem + 1) << 8;
+    if (dev >= 0 && dev < 64) {
+        const unsigned long long c = cache[dev].load(std::memory_order_relaxed);
+        if ((c & ~0xFFull) == key) return (int)(c & 0xFF);
+    }
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_gemv_kernel<T, MT, KS, PRO, EPI>, 256, smem) !=
+            cudaSuccess ||
+        n < 1) {
+        cudaGetLastError();
+        n = 1;
+    }
+    n = n > kCtasPerSM ? kCtasPerSM : n;
+    if (dev >= 0 && dev < 64) cache[dev].store(key | (unsigned long long)n, std::memory_order_relaxed);
+    return n;
+}
+
 template <typename T, int MT, int KS, int PRO, int EPI>
 int launch_one(const DecodeGemvParams &p, cudaStream_t s) {
     constexpr int GROUPS = 8 / KS;
     const int nblocks = (p.groups + GROUPS - 1) / GROUPS;
-    const int cap = sm_count() * kCtasPerSM;  // persistent: each CTA loops over weight-row blocks
-    const int blocks = nblocks < cap ? nblocks : cap;
     const size_t smem = PRO == PRO_RMS ? (size_t)MT * p.K * sizeof(T) : 0;
+    // persistent: as many CTAs as can be resident at once (registers decide:
+    // 72-116 per thread give 2-3 CTAs of 256 threads per SM), each looping
+    // over weight-row blocks, so no CTA waits for another to retire
+    const int cap = sm_count() * resident_ctas<T, MT, KS, PRO, EPI>(smem);
+    const int blocks = nblocks < cap ? nblocks : cap;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)blocks);
     cfg.blockDim = dim3(256);
@@ -243,6 +304,14 @@ int launch_ks(const DecodeGemvParams &p, cudaStream_t s) {
     while (ks < 8 && (nvec + ks - 1) / ks > 32 * kVPL) ks *= 2;
     while (ks < 8 && (p.groups + 8 / ks - 1) / (8 / ks) < 2 * sm_count() && (nvec + 2 * ks - 1) / (2 * ks) >= 32)
         ks *= 2;
+    // ... but not past the point where the blocks no longer fit in one wave
+    // of resident CTAs when half the split would: a second wave costs a
+    // whole extra HBM round trip for a few CTAs
+    const size_t smem = PRO == PRO_RMS ? (size_t)MT * p.K * sizeof(T) : 0;
+    const int ctas = sm_count() * resident_ctas<T, MT, 8, PRO, EPI>(smem);
+    auto blocks = [&](int k) { return (p.groups + 8 / k - 1) / (8 / k); };
+    while (ks > 1 && blocks(ks) > ctas && blocks(ks / 2) <= ctas && (nvec + ks / 2 - 1) / (ks / 2) <= 32 * kVPL)
+        ks /= 2;
     switch (ks) {
     case 1: return launch_one<T, MT, 1, PRO, EPI>(p, s);
     case 2: return launch_one<T, MT, 2, PRO, EPI>(p, s);
@@ -261,6 +330,8 @@ int launch_mt(const DecodeGemvParams &p, cudaStream_t s) {
 
 template <typename T>
 int dispatch(const DecodeGemvParams &p0, int pro, int epi, cudaStream_t s) {
+    WGB_REQUIRE(p0.K > 0 && p0.K % Vec16<T>::N == 0, WGB_ERR_INVALID_ARGUMENT,
+                "decode_gemv: K = %d is not a whole number of 16-byte vectors", p0.K);
     // more than 8 rows of bf16: one tensor-core GEMM over all rows (the RMS
     // prologue first materialised into p0.xn)
     if (std::is_same<T, __nv_bfloat16>::value && p0.M0 > kMaxMT && (pro == PRO_PLAIN || p0.xn)) {
@@ -329,6 +400,9 @@ void decode_gemv_prepare() {
 }
 
 int decode_gemv(wginferDataType_t dtype, const DecodeGemvParams &p, int pro, int epi, cudaStream_t s) {
+    // 16-byte vectors throughout: weights, input rows and the norm weight
+    WGB_REQUIRE(aligned16(p.w) && aligned16(p.x) && (pro != PRO_RMS || aligned16(p.norm_w)), WGB_ERR_INVALID_ARGUMENT,
+                "decode_gemv: operands must be 16-byte aligned");
     WGB_DISPATCH_FLOAT(dtype, T, return dispatch<T>(p, pro, epi, s));
     return WGB_OK;
 }

@@ -34,7 +34,7 @@ constexpr int kTcThreads = 128;
 constexpr int kBK = 64;          // K elements per stage (128 bytes of bf16: one swizzle span)
 constexpr int kTcStages = 4;
 constexpr int kTileW = 128;      // weight rows per CTA (MMA M)
-constexpr uint64_t kTcWaitNs = 2000000000ull;  // a ring stage stalled this long counts as a failure
+constexpr long long kTcWaitCycles = 4000000000ll;  // a stage stalled this long (about 2 s) counts as a failure
 
 __device__ __forceinline__ uint32_t s_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -44,14 +44,11 @@ __device__ __forceinline__ void mb_init(uint64_t *b, unsigned n) {
 __device__ __forceinline__ void mb_expect_tx(uint64_t *b, unsigned bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_u32(b)), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-// Bounded wait for the phase with the given parity: false after kTcWaitNs.
+// Bounded wait for the phase with the given parity: polls first, then
+// checks the SM cycle counter (cheap, unlike %globaltimer) every 64 polls;
+// false after kTcWaitCycles.
 __device__ __forceinline__ bool mb_wait(uint64_t *b, unsigned parity) {
-    uint64_t t0 = 0;
+    long long t0 = 0;
     for (unsigned i = 0;; i++) {
         unsigned ok;
         asm volatile(
@@ -60,10 +57,10 @@ __device__ __forceinline__ bool mb_wait(uint64_t *b, unsigned parity) {
             : "r"(s_u32(b)), "r"(parity)
             : "memory");
         if (ok) return true;
-        if ((i & 255) == 0) {
-            const uint64_t t = global_ns();
-            if (i == 0) t0 = t;
-            else if (t - t0 > kTcWaitNs) return false;
+        if ((i & 63) == 63) {
+            const long long t = clock64();
+            if (i == 63) t0 = t;
+            else if (t - t0 > kTcWaitCycles) return false;
         }
     }
 }
