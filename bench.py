@@ -179,35 +179,59 @@ def time_decode(m, batch, K, W, world):
     return e0.elapsed_time(e1) / 1e3
 
 
-def gemv_roofline(w_out, hs, voc, peak, K=20):
-    """Times the lm_head GEMV (the largest weight-streaming launch, [1,1536] x
-    [151936,1536]^T) live with CUDA events on the launching stream."""
+def _time_linear(out, x, ws, K):
+    """Average device time (s) of K ops.linear launches cycling through `ws`,
+    CUDA events on the launching stream."""
     import torch
     from wginfer_b200 import numerics, ops
-    x = torch.randn(1, hs, device=w_out.device).to(w_out.dtype)
-    out = torch.empty(1, voc, device=w_out.device, dtype=w_out.dtype)
     with numerics("fast"):
-        for _ in range(3):
-            ops.linear(out, x, w_out)
+        for i in range(3):
+            ops.linear(out, x, ws[i % len(ws)])
         s = torch.cuda.current_stream()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
         e0.record(s)
-        for _ in range(K):
-            ops.linear(out, x, w_out)
+        for i in range(K):
+            ops.linear(out, x, ws[i % len(ws)])
         e1.record(s)
         e1.synchronize()
-    dt = e0.elapsed_time(e1) / 1e3 / K
-    nbytes = (voc * hs + hs + voc) * w_out.element_size()
-    achieved = nbytes / dt / 1e9
+    return e0.elapsed_time(e1) / 1e3 / K
+
+
+def gemv_roofline(w_out, cfg, peak, K=24):
+    """Roofline of the dominant decode kernel: the weight-streaming GEMV of the
+    gate/up projection ([1,1536] x [17920,1536]^T, 55 MB of bf16 weights, 28%
+    of a decode step's kernel time), timed live with CUDA events over eight
+    weight copies (440 MB, so every launch streams from HBM, not L2). The
+    lm_head GEMV ([1,1536] x [151936,1536]^T) is reported beside it."""
+    import torch
+    dev, dt = w_out.device, w_out.dtype
+    g = torch.Generator(device=dev).manual_seed(7)
+    n_gu, k = 2 * cfg.di, cfg.hs
+    ws = [(torch.randn(n_gu, k, device=dev, generator=g) * 0.02).to(dt) for _ in range(8)]
+    x = torch.randn(1, k, device=dev, generator=g).to(dt)
+    out = torch.empty(1, n_gu, device=dev, dtype=dt)
+    dt_gu = _time_linear(out, x, ws, K)
+    del ws
+    nbytes = (n_gu * k + k + n_gu) * w_out.element_size()
     traffic = None
     try:
-        prof = json.load(open(os.path.join(ROOT, "profiles", "gemv_lm_head_traffic.json")))
-        traffic = prof.get("dram_bytes_per_launch")
+        prof = json.load(open(os.path.join(ROOT, "profiles", "gemv_traffic.json")))
+        traffic = prof.get("gate_up", {}).get("dram_bytes_per_launch")
+        traffic_lm = prof.get("lm_head", {}).get("dram_bytes_per_launch")
     except Exception:
-        pass
-    return {"kernel": "gemv_kernel (lm_head [1,1536]x[151936,1536]^T, bf16)", "bound": "hbm",
+        traffic_lm = None
+    xl = torch.randn(1, cfg.hs, device=dev, generator=g).to(dt)
+    ol = torch.empty(1, cfg.voc, device=dev, dtype=dt)
+    dt_lm = _time_linear(ol, xl, [w_out], 20)
+    nbytes_lm = (cfg.voc * cfg.hs + cfg.hs + cfg.voc) * w_out.element_size()
+    achieved = nbytes / dt_gu / 1e9
+    return {"kernel": "decode_gemv_kernel (gate/up projection [1,1536]x[17920,1536]^T, bf16)", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-            "traffic": traffic, "algorithmic_bytes": nbytes, "us_per_launch": round(dt * 1e6, 2)}
+            "traffic": traffic, "algorithmic_bytes": nbytes, "us_per_launch": round(dt_gu * 1e6, 2),
+            "lm_head": {"achieved": round(nbytes_lm / dt_lm / 1e9, 1), "frac": round(nbytes_lm / dt_lm / 1e9 / peak, 4),
+                        "algorithmic_bytes": nbytes_lm, "us_per_launch": round(dt_lm * 1e6, 2),
+                        "traffic": traffic_lm}}
 
 
 def run_b200(args):
@@ -245,7 +269,7 @@ def run_b200(args):
         e1.synchronize()
         barrier(world)
         te = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
-        roof = gemv_roofline(kept["out_embed"], cfg.hs, cfg.voc, peak)
+        roof = gemv_roofline(kept["out_embed"], cfg, peak)
         roof["peak_source"] = peak_src
         del kept
         m.close()

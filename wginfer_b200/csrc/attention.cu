@@ -491,9 +491,11 @@ __global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict
 template <typename T, int DH, class Src>
 int launch_warp_attn(T *out, const T *q, Src src, const AttnShape &sh, cudaStream_t s, const void *pf_ptr,
                      size_t pf_bytes) {
-    // slices: enough CTAs per head to give each warp about one 32-key chunk
+    // slices: at most 3 chunks of 32 keys per CTA, so that a head's work is
+    // spread over up to 8 SMs (the per-warp dot and P.V are latency-bound;
+    // fewer busy warps per SM finish them sooner)
     const int chunks = (sh.L + kWarpKeys - 1) / kWarpKeys;
-    int ns = (chunks + 7) / 8;
+    int ns = (chunks + 2) / 3;
     if (ns > kMaxCluster) ns = kMaxCluster;
     if (ns < 1) ns = 1;
     cudaLaunchConfig_t cfg = {};

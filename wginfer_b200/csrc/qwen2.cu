@@ -345,8 +345,8 @@ int run_layer_fast(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t to
     p.xn = M->xn;
     if ((rc = decode_gemv(M->dt, p, DG_PRO_RMS, DG_EPI_ROPEKV, s))) return rc;
     WGB_TRACE("qkv_gemv+rms+rope+kv");
-    if ((rc = attention(M, l, T, prefill_seq, total_len, false, (const char *)w.gu_w + gu_b / 2, gu_b / 2)))
-        return rc;
+    // no L2 prefetch from attention: its own K/V reads are latency-critical
+    if ((rc = attention(M, l, T, prefill_seq, total_len, false))) return rc;
     WGB_TRACE("attention");
     // o_proj + residual
     DecodeGemvParams o{};
