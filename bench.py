@@ -93,34 +93,19 @@ class Clocks:
 
 # ---------------------------------------------------------------- helpers
 def dist_setup(n_gpus):
-    import torch
-    import torch.distributed as dist
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        from datetime import timedelta
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
-    elif torch.cuda.is_available():
-        torch.cuda.set_device(0)
-    return world, rank, local
+    """One process per GPU under torchrun (NCCL), else a single GPU."""
+    from wginfer_b200 import dist as D
+    return D.setup(timeout_s=300.0)
 
 
 def barrier(world):
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
+    from wginfer_b200 import dist as D
+    D.barrier()
 
 
 def max_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from wginfer_b200 import dist as D
+    return D.max_over_ranks(x)
 
 
 def device_weights(cfg, seed, device):
@@ -180,21 +165,30 @@ def time_decode(m, batch, K, W, world):
 
 
 def _time_linear(out, x, ws, K):
-    """Average device time (s) of K ops.linear launches cycling through `ws`,
-    CUDA events on the launching stream."""
+    """Average device time (s) of one ops.linear launch: K launches cycling
+    through `ws` are captured once in a CUDA graph (so host launch overhead
+    leaves no gaps between them) and the replay is timed with CUDA events on
+    the capturing stream."""
     import torch
     from wginfer_b200 import numerics, ops
+    s = torch.cuda.Stream()
     with numerics("fast"):
-        for i in range(3):
-            ops.linear(out, x, ws[i % len(ws)])
-        s = torch.cuda.current_stream()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            for i in range(3):
+                ops.linear(out, x, ws[i % len(ws)])
         torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(K):
+                ops.linear(out, x, ws[i % len(ws)])
+    with torch.cuda.stream(s):
+        g.replay()  # warm
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s)
-        for i in range(K):
-            ops.linear(out, x, ws[i % len(ws)])
+        g.replay()
         e1.record(s)
-        e1.synchronize()
+    e1.synchronize()
+    del g
     return e0.elapsed_time(e1) / 1e3 / K
 
 
@@ -232,6 +226,14 @@ def gemv_roofline(w_out, cfg, peak, K=24):
             "lm_head": {"achieved": round(nbytes_lm / dt_lm / 1e9, 1), "frac": round(nbytes_lm / dt_lm / 1e9 / peak, 4),
                         "algorithmic_bytes": nbytes_lm, "us_per_launch": round(dt_lm * 1e6, 2),
                         "traffic": traffic_lm}}
+
+
+def decode_config(args, world):
+    """The workload both arms report (the metric is quoted on it)."""
+    return {"workload": "Qwen2-1.5B arch (28 layers, hidden 1536, 12/2 heads x 128, MLP 8960, vocab "
+                        "151936), greedy decode, batch 1 per GPU, prompt %d" % args.prompt,
+            "global_batch": world, "seq_len": args.prompt + args.steps, "parallelism": f"replicas x{world}",
+            "numerics": args.numerics, "l2": "weights 3.1 GB > L2; no flush needed"}
 
 
 def run_b200(args):
@@ -277,10 +279,7 @@ def run_b200(args):
     bytes_per_token = cfg.weight_bytes()
     result.update({
         "value": round(value, 2), "ms_per_step": round(t_max / K * 1e3, 4),
-        "config": {"workload": "Qwen2-1.5B arch (28 layers, hidden 1536, 12/2 heads x 128, MLP 8960, vocab "
-                               "151936), greedy decode, batch 1 per GPU, prompt %d" % args.prompt,
-                   "global_batch": world, "seq_len": args.prompt + K, "parallelism": f"replicas x{world}",
-                   "numerics": args.numerics, "l2": "weights 3.1 GB > L2; no flush needed"},
+        "config": decode_config(args, world),
         "weight_stream_roofline": {"bytes_per_token": bytes_per_token,
                                    "tok_s_at_peak": round(peak * 1e9 / bytes_per_token, 1),
                                    "frac": round(value / world / (peak * 1e9 / bytes_per_token), 4)},
@@ -308,16 +307,18 @@ def bs64(args, world, rank, local):
     one-layer model; each GPU holds 64/N of them."""
     from wginfer_b200 import numerics
     from wginfer_b200.synthetic import Qwen2Config, prompt_ids
+    from wginfer_b200 import dist as D
     total = 64
-    per = total // world
+    mine = D.partition(total, world, rank)  # this GPU's requests
+    per = len(mine)
     K, W = min(args.steps, 200), min(args.warmup, 8)
     cfg = Qwen2Config(nlayer=1, maxseq=2048 + 256)
     with numerics(args.numerics):
         m, _ = build_model(cfg, per, local, seed=0)
         ids = prompt_ids(2048, cfg.voc, seed=1000, batch=total).numpy()
         t0 = time.time()
-        for b in range(per):
-            m.prefill(b, ids[rank * per + b])
+        for b, i in enumerate(mine):
+            m.prefill(b, ids[i])
         prefill_s = time.time() - t0
         t = time_decode(m, per, K, W, world)
         m.close()
@@ -399,11 +400,11 @@ def run_reference(args):
            "steps": len(per), "warmup": min(args.warmup, 1), "ms_per_step": round(t / len(per) * 1e3, 2),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
            "data": "synthetic (seeded random weights)",
-           "config": {"workload": "Qwen2-1.5B arch greedy decode, batch 1 (reference Model::infer on the CPU "
-                                  "device)", "global_batch": 1, "seq_len": 2, "parallelism": "none"},
+           "config": decode_config(args, world),
            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "reference",
-                            "sample": "per step one decode token on 1- and 2-layer reference models of the full "
-                                      "dimensions; 28-layer time = t1 + 27 (t2 - t1)"},
+                            "sample": "per step one decode token of the reference Model::infer (oracle/_ref, "
+                                      "its CPU device) on 1- and 2-layer models of the full dimensions at a short "
+                                      "cache; 28-layer time = t1 + 27 (t2 - t1)"},
            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
