@@ -228,6 +228,93 @@ def gemv_roofline(w_out, cfg, peak, K=24):
                         "traffic": traffic_lm}}
 
 
+def _graph_time(fn, reps):
+    """Average device time (s) of fn(i) over `reps` calls captured in one
+    CUDA graph, timed with CUDA events around a replay (after a warm replay)."""
+    import torch
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for i in range(2):
+            fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(reps):
+            fn(i)
+    with torch.cuda.stream(s):
+        g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+    e1.synchronize()
+    del g
+    return e0.elapsed_time(e1) / 1e3 / reps
+
+
+def op_sweep(peak, quick=False):
+    """Bandwidth sweep of the elementwise and reduction ops (add, swiglu on
+    flat tensors of 1M..1G elements; rms_norm rows of 1536/4096/8192; argmax
+    over [B, 151936]), bf16 and f32, inputs ~N(0,1). Each case cycles through
+    enough copies of its operands that every launch streams more than L2
+    (126 MB) from HBM; achieved = algorithmic bytes / device time."""
+    import torch
+    from wginfer_b200 import numerics, ops
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    L2_SPAN = 256 << 20
+    out = []
+
+    def copies(bytes_per_iter, budget=6 << 30):
+        return int(max(1, min(64, -(-L2_SPAN // bytes_per_iter), budget // bytes_per_iter)))
+
+    def record(op, dtype, shape, nbytes, t):
+        gbs = nbytes / t / 1e9
+        out.append({"op": op, "dtype": dtype, "shape": shape, "bytes": nbytes, "us": round(t * 1e6, 2),
+                    "gbs": round(gbs, 1), "frac": round(gbs / peak, 3)})
+
+    flat = [1 << 20, 1 << 24, 1 << 28] + ([] if quick else [1 << 30])
+    with numerics("fast"):
+        for tdt, name in ((torch.bfloat16, "bf16"), (torch.float32, "f32")):
+            es = torch.tensor([], dtype=tdt).element_size()
+            for n in flat:
+                per = 3 * n * es
+                if per > (16 << 30):
+                    continue
+                nc = copies(per)
+                a = [torch.randn(n, device="cuda", generator=gen).to(tdt) for _ in range(nc)]
+                b = [torch.randn(n, device="cuda", generator=gen).to(tdt) for _ in range(nc)]
+                c = [torch.empty(n, device="cuda", dtype=tdt) for _ in range(nc)]
+                reps = max(3, min(100, (2 << 30) // per))
+                record("add", name, [n], per, _graph_time(lambda i: ops.add(c[i % nc], a[i % nc], b[i % nc]), reps))
+                record("swiglu", name, [1, n], per, _graph_time(
+                    lambda i: ops.swiglu(c[i % nc].view(1, -1), a[i % nc].view(1, -1), b[i % nc].view(1, -1)), reps))
+                del a, b, c
+            for h in (1536, 4096, 8192):
+                rows = (256 << 20) // (h * es)
+                per = 2 * rows * h * es + h * es
+                nc = copies(per)
+                x = [torch.randn(rows, h, device="cuda", generator=gen).to(tdt) for _ in range(nc)]
+                y = [torch.empty(rows, h, device="cuda", dtype=tdt) for _ in range(nc)]
+                w = (torch.randn(h, device="cuda", generator=gen) * 0.1 + 1).to(tdt)
+                record("rms_norm", name, [rows, h], per,
+                       _graph_time(lambda i: ops.rms_norm(y[i % nc], x[i % nc], w, 1e-6), 20))
+                del x, y
+            for B in (1, 16, 64, 256):
+                V = 151936
+                per = B * V * es + B * (8 + es)
+                nc = copies(per)
+                v = [torch.randn(B, V, device="cuda", generator=gen).to(tdt) for _ in range(nc)]
+                idx = torch.empty(B, dtype=torch.int64, device="cuda")
+                val = torch.empty(B, dtype=tdt, device="cuda")
+                record("argmax", name, [B, V], per,
+                       _graph_time(lambda i: ops.argmax_rows(idx, val, v[i % nc]), max(3, min(100, (2 << 30) // per))))
+                del v
+    torch.cuda.empty_cache()
+    big = [r for r in out if r["bytes"] >= (64 << 20)]
+    return {"unit": "GB/s", "peak": peak, "cases": out,
+            "min_frac_at_64MB_or_more": round(min(r["frac"] for r in big), 3) if big else None}
+
+
 def decode_config(args, world):
     """The workload both arms report (the metric is quoted on it)."""
     return {"workload": "Qwen2-1.5B arch (28 layers, hidden 1536, 12/2 heads x 128, MLP 8960, vocab "
@@ -293,6 +380,8 @@ def run_b200(args):
     })
     if not args.no_bs64:
         result["bs64"] = bs64(args, world, rank, local)
+    if rank == 0 and not args.no_sweep:
+        result["op_bandwidth"] = op_sweep(peak, quick=world > 1)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if world > 1:
@@ -419,6 +508,7 @@ def main():
     ap.add_argument("--numerics", default="fast", choices=["fast", "reference"])
     ap.add_argument("--no-bs64", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the elementwise/reduction bandwidth sweep")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--ref-max-steps", type=int, default=12)
     args = ap.parse_args()

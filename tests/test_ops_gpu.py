@@ -131,6 +131,33 @@ def test_argmax_nan_semantics(oracle, cuda):
     assert idx.item() == 2 and val.item() == 3.0
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16, torch.float32])
+def test_argmax_rows_special_values(oracle, cuda, dt):
+    """Vectorised rows with NaNs, signed-zero maxima, -inf rows, all-NaN rows
+    and ties inside one 16-byte vector, against the oracle's sequential scan
+    (argmax_cpu.cpp:26-47)."""
+    n = 4096
+    g = torch.Generator("cpu").manual_seed(3)
+    rows = []
+    r = -torch.rand(n, generator=g) - 1.0; r[100] = 0.0; r[50] = -0.0; rows.append(r)  # -0 first, then +0
+    r = torch.randn(n, generator=g); r[0:8] = float("nan"); r[9] = 9.0; r[10] = 9.0; rows.append(r)  # tie in a vector
+    r = torch.full((n,), float("-inf")); rows.append(r)  # nothing beats -inf: index 0
+    r = torch.full((n,), float("nan")); r[4000] = -5.0; rows.append(r)  # the only number
+    r = torch.full((n,), float("nan")); rows.append(r)  # all NaN: index 0
+    r = torch.randn(n, generator=g); r[0] = float("nan"); rows.append(r)  # NaN at index 0 wins
+    r = torch.randn(n, generator=g); r[17] = float("inf"); r[4095] = float("inf"); rows.append(r)
+    vals = torch.stack(rows).to(dt).cuda()
+    idx = torch.empty(len(rows), dtype=torch.int64, device="cuda")
+    val = torch.empty(len(rows), dtype=dt, device="cuda")
+    ops.argmax_rows(idx, val, vals)
+    code = {torch.bfloat16: 15, torch.float16: 12, torch.float32: 13}[dt]
+    host = vals.cpu()
+    for i in range(len(rows)):
+        row = host[i].numpy() if dt == torch.float32 else host[i].view(torch.int16).numpy().view(np.uint16)
+        want_i, _ = oracle.argmax(np.ascontiguousarray(row), code)
+        assert idx[i].item() == want_i, (i, idx[i].item(), want_i)
+
+
 def test_embedding_out_of_range_is_recorded(cuda):
     w = _bf16((16, 64), 9)
     out = torch.full((3, 64), 7.0, dtype=torch.bfloat16, device="cuda")

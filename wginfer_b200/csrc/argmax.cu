@@ -1,7 +1,8 @@
 // argmax over each row of vals[rows, numel]: the first index of the maximum
 // under '>' in f32 (src/ops/argmax/cpu/argmax_cpu.cpp:26-47), bit-exact.
 //
-// A thread-block cluster of kCluster CTAs shares one row: each CTA reduces
+// A thread-block cluster of up to 8 CTAs shares one row (fewer when there are
+// many rows, so that all CTAs fit in one wave): each CTA reduces
 // its slice with 16-byte loads to one 64-bit key per CTA, and CTA 0 of the
 // cluster folds the keys of the others through distributed shared memory,
 // so no global scratch and no second launch are needed. Key = (order-
@@ -11,6 +12,8 @@
 // where the sequential scan keeps it, as the reference does.
 // Roofline: HBM, rows*numel*size + rows*(8+size) bytes.
 #include <cooperative_groups.h>
+
+#include <atomic>
 
 #include "common.cuh"
 
@@ -29,51 +32,80 @@ __device__ __forceinline__ unsigned long long make_key(float v, uint32_t idx) {
     return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
 }
 
+// Per-thread running best over the thread's elements, which it visits in
+// increasing index order: strict '>' keeps the first index of a tie, and NaN
+// never compares greater. The 64-bit key is formed only when threads merge.
+struct Best {
+    float v;
+    uint32_t i;  // 0xFFFFFFFF: nothing seen yet
+};
 template <typename T>
-__device__ __forceinline__ void consider(unsigned long long &best, T x, uint32_t idx) {
-    float v = Elem<T>::load(x);
-    if (!isnan(v)) {
-        unsigned long long k = make_key(v, idx);
-        best = k > best ? k : best;
+__device__ __forceinline__ void consider(Best &b, T x, uint32_t idx) {
+    const float v = Elem<T>::load(x);
+    if (v > b.v || (b.i == 0xFFFFFFFFu && !isnan(v))) {
+        b.v = v;
+        b.i = idx;
     }
+}
+// Maximum of a 16-byte vector (NaN ignored unless every element is NaN).
+template <typename T> __device__ __forceinline__ float vec_max(const Vec16<T> &r);
+template <> __device__ __forceinline__ float vec_max<__nv_bfloat16>(const Vec16<__nv_bfloat16> &r) {
+    const __nv_bfloat162 *p = reinterpret_cast<const __nv_bfloat162 *>(&r.u);
+    const __nv_bfloat162 m = __hmax2(__hmax2(p[0], p[1]), __hmax2(p[2], p[3]));
+    return fmaxf(__low2float(m), __high2float(m));
+}
+template <> __device__ __forceinline__ float vec_max<__half>(const Vec16<__half> &r) {
+    const __half2 *p = reinterpret_cast<const __half2 *>(&r.u);
+    const __half2 m = __hmax2(__hmax2(p[0], p[1]), __hmax2(p[2], p[3]));
+    return fmaxf(__low2float(m), __high2float(m));
+}
+// A whole vector: 16-bit types compare the vector's maximum first and scan
+// the elements (in index order, as above) only when it beats the running
+// best, which is exactly when a scan could change it.
+template <typename T>
+__device__ __forceinline__ void consider_vec(Best &b, const Vec16<T> &r, uint32_t idx0) {
+    constexpr int V = Vec16<T>::N;
+    if constexpr (sizeof(T) == 2) {
+        const float vm = vec_max<T>(r);
+        if (!(vm > b.v || (b.i == 0xFFFFFFFFu && !isnan(vm)))) return;
+    }
+#pragma unroll
+    for (int e = 0; e < V; e++) consider(b, r.e[e], idx0 + e);
 }
 
 template <typename T, bool kVec>
-__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
-    argmax_cluster_kernel(int64_t *max_idx, T *max_val, const T *vals, size_t numel) {
+__global__ void __launch_bounds__(kThreads) argmax_cluster_kernel(int64_t *max_idx, T *max_val, const T *vals,
+                                                                  size_t numel) {
     constexpr int V = Vec16<T>::N;
     __shared__ unsigned long long red[kThreads / 32];
     cg::cluster_group cluster = cg::this_cluster();
-    const unsigned rank = cluster.block_rank();
-    const size_t row = blockIdx.x / kCluster;
+    const unsigned rank = cluster.block_rank(), ns = cluster.num_blocks();
+    const size_t row = blockIdx.x / ns;
     const T *x = vals + row * numel;
-    unsigned long long best = 0ull;  // below every real key
+    Best bt{-INFINITY, 0xFFFFFFFFu};
 
     if (kVec) {
         const size_t nvec = numel / V;
-        const size_t per = (nvec + kCluster - 1) / kCluster;
-        const size_t v0 = rank * per, v1 = v0 + per < nvec ? v0 + per : nvec;
-        size_t i = v0 + threadIdx.x;
-        for (; i + 3 * kThreads < v1; i += 4 * kThreads) {
-            Vec16<T> r[4];
+        const size_t per = (nvec + ns - 1) / ns;
+        const size_t v0 = rank * per < nvec ? rank * per : nvec, v1 = v0 + per < nvec ? v0 + per : nvec;
+        // batches of 8 vectors per thread, the last batch predicated, so a
+        // thread's slice costs ceil(slice / 8) round trips
+        constexpr int kB = 8;
+        for (size_t i = v0 + threadIdx.x; i < v1; i += kB * kThreads) {
+            Vec16<T> r[kB];
 #pragma unroll
-            for (int u = 0; u < 4; u++) r[u].u = ld_global_nc_v4(x + (i + u * kThreads) * V);
+            for (int u = 0; u < kB; u++)
+                if (i + u * kThreads < v1) r[u].u = ld_global_nc_v4(x + (i + u * kThreads) * V);
 #pragma unroll
-            for (int u = 0; u < 4; u++)
-#pragma unroll
-                for (int e = 0; e < V; e++) consider(best, r[u].e[e], (uint32_t)((i + u * kThreads) * V + e));
-        }
-        for (; i < v1; i += kThreads) {
-            Vec16<T> r;
-            r.u = ld_global_nc_v4(x + i * V);
-#pragma unroll
-            for (int e = 0; e < V; e++) consider(best, r.e[e], (uint32_t)(i * V + e));
+            for (int u = 0; u < kB; u++)
+                if (i + u * kThreads < v1) consider_vec(bt, r[u], (uint32_t)((i + u * kThreads) * V));
         }
     } else {
-        const size_t per = (numel + kCluster - 1) / kCluster;
-        const size_t e0 = rank * per, e1 = e0 + per < numel ? e0 + per : numel;
-        for (size_t i = e0 + threadIdx.x; i < e1; i += kThreads) consider(best, x[i], (uint32_t)i);
+        const size_t per = (numel + ns - 1) / ns;
+        const size_t e0 = rank * per < numel ? rank * per : numel, e1 = e0 + per < numel ? e0 + per : numel;
+        for (size_t i = e0 + threadIdx.x; i < e1; i += kThreads) consider(bt, x[i], (uint32_t)i);
     }
+    unsigned long long best = bt.i == 0xFFFFFFFFu ? 0ull : make_key(bt.v, bt.i);  // 0: below every real key
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
@@ -93,7 +125,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     cluster.sync();  // every CTA's red[0] is final and visible cluster-wide
     if (rank == 0 && threadIdx.x == 0) {
         unsigned long long b = red[0];
-        for (unsigned r = 1; r < kCluster; r++) {
+        for (unsigned r = 1; r < ns; r++) {
             unsigned long long o = *cluster.map_shared_rank(&red[0], r);
             b = o > b ? o : b;
         }
@@ -115,9 +147,41 @@ template <typename T>
 int launch_argmax(int64_t *idx, T *val, const T *vals, size_t rows, size_t numel, cudaStream_t s) {
     constexpr int V = Vec16<T>::N;
     const bool vec = aligned16(vals) && (numel % V) == 0;
-    dim3 grid((unsigned)(rows * kCluster));
-    if (vec) argmax_cluster_kernel<T, true><<<grid, kThreads, 0, s>>>(idx, val, vals, numel);
-    else argmax_cluster_kernel<T, false><<<grid, kThreads, 0, s>>>(idx, val, vals, numel);
+    // CTAs per row: up to kCluster, but no more than one wave of resident
+    // CTAs over all rows (the resident count comes from the occupancy query,
+    // cached per device and variant)
+    static std::atomic<int> resident[64][2];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int per_sm = dev >= 0 && dev < 64 ? resident[dev][vec ? 1 : 0].load(std::memory_order_relaxed) : 0;
+    if (per_sm <= 0) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                &per_sm, vec ? argmax_cluster_kernel<T, true> : argmax_cluster_kernel<T, false>, kThreads, 0) !=
+                cudaSuccess ||
+            per_sm < 1) {
+            cudaGetLastError();
+            per_sm = 1;
+        }
+        if (dev >= 0 && dev < 64) resident[dev][vec ? 1 : 0].store(per_sm, std::memory_order_relaxed);
+    }
+    const size_t wave = (size_t)sm_count() * per_sm;
+    size_t ns = rows >= wave ? 1 : wave / rows;
+    if (ns > (size_t)kCluster) ns = kCluster;
+    if (ns < 1) ns = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(rows * ns));
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = (unsigned)ns;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true>, idx, val, vals, numel)
+                        : cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, false>, idx, val, vals, numel);
+    if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "wgb_argmax: %s", cudaGetErrorString(e));
     return check_launch("wgb_argmax");
 }
 

@@ -1,7 +1,7 @@
 // rms_norm: y = x * w * (mean(x^2) + eps)^-1/2 per row.
 //
 // FAST: the row is read from HBM once into registers with 16-byte loads (a
-// warp per row up to 256 vectors, a 256-thread CTA per row up to 1024
+// warp per row up to 256 vectors, a 256-thread CTA per row up to 2048
 // vectors), squares are summed in f32 with warp shuffles, and the scaled
 // row is written from the same registers. Other sizes or unaligned views use
 // a two-pass CTA-per-row kernel (second read hits L2).
@@ -30,13 +30,20 @@ __global__ void __launch_bounds__(256) rms_warp_kernel(T *__restrict__ out, cons
     if (row >= M) return;
     const int nvec = N / V;
     const T *x = in + (size_t)row * N;
-    Vec16<T> r[VPL];
+    Vec16<T> r[VPL], wr[VPL];
     float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < VPL; u++) {  // x and the norm weight in one round trip
+        int vi = lane + u * 32;
+        if (vi < nvec) {
+            r[u].u = ld_global_nc_v4(x + (size_t)vi * V);
+            wr[u].u = ld_global_nc_v4(w + (size_t)vi * V);
+        }
+    }
 #pragma unroll
     for (int u = 0; u < VPL; u++) {
         int vi = lane + u * 32;
         if (vi < nvec) {
-            r[u].u = ld_global_nc_v4(x + (size_t)vi * V);
 #pragma unroll
             for (int e = 0; e < V; e++) {
                 float f = Elem<T>::load(r[u].e[e]);
@@ -51,11 +58,10 @@ __global__ void __launch_bounds__(256) rms_warp_kernel(T *__restrict__ out, cons
     for (int u = 0; u < VPL; u++) {
         int vi = lane + u * 32;
         if (vi < nvec) {
-            Vec16<T> wv, o;
-            wv.u = ld_global_nc_v4(w + (size_t)vi * V);
+            Vec16<T> o;
 #pragma unroll
             for (int e = 0; e < V; e++)
-                o.e[e] = Elem<T>::store(__fmul_rn(__fmul_rn(Elem<T>::load(r[u].e[e]), Elem<T>::load(wv.e[e])), sc));
+                o.e[e] = Elem<T>::store(__fmul_rn(__fmul_rn(Elem<T>::load(r[u].e[e]), Elem<T>::load(wr[u].e[e])), sc));
             *reinterpret_cast<uint4 *>(y + (size_t)vi * V) = o.u;
         }
     }
@@ -69,13 +75,20 @@ __global__ void __launch_bounds__(256) rms_block_kernel(T *__restrict__ out, con
     const int row = blockIdx.x;
     const int nvec = N / V;
     const T *x = in + (size_t)row * N;
-    Vec16<T> r[VPT];
+    Vec16<T> r[VPT], wr[VPT];
     float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < VPT; u++) {  // x and the norm weight in one round trip
+        int vi = threadIdx.x + u * 256;
+        if (vi < nvec) {
+            r[u].u = ld_global_nc_v4(x + (size_t)vi * V);
+            wr[u].u = ld_global_nc_v4(w + (size_t)vi * V);
+        }
+    }
 #pragma unroll
     for (int u = 0; u < VPT; u++) {
         int vi = threadIdx.x + u * 256;
         if (vi < nvec) {
-            r[u].u = ld_global_nc_v4(x + (size_t)vi * V);
 #pragma unroll
             for (int e = 0; e < V; e++) {
                 float f = Elem<T>::load(r[u].e[e]);
@@ -94,11 +107,10 @@ __global__ void __launch_bounds__(256) rms_block_kernel(T *__restrict__ out, con
     for (int u = 0; u < VPT; u++) {
         int vi = threadIdx.x + u * 256;
         if (vi < nvec) {
-            Vec16<T> wv, o;
-            wv.u = ld_global_nc_v4(w + (size_t)vi * V);
+            Vec16<T> o;
 #pragma unroll
             for (int e = 0; e < V; e++)
-                o.e[e] = Elem<T>::store(__fmul_rn(__fmul_rn(Elem<T>::load(r[u].e[e]), Elem<T>::load(wv.e[e])), sc));
+                o.e[e] = Elem<T>::store(__fmul_rn(__fmul_rn(Elem<T>::load(r[u].e[e]), Elem<T>::load(wr[u].e[e])), sc));
             *reinterpret_cast<uint4 *>(y + (size_t)vi * V) = o.u;
         }
     }
@@ -177,10 +189,12 @@ int launch_rms(T *out, const T *in, const T *w, size_t M, size_t N, float eps, c
         int blocks = (int)((M + 7) / 8);
         if (nvec <= 32 * 2) rms_warp_kernel<T, 2><<<blocks, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
         else if (nvec <= 32 * 4) rms_warp_kernel<T, 4><<<blocks, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
+        else if (nvec <= 32 * 6) rms_warp_kernel<T, 6><<<blocks, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
         else rms_warp_kernel<T, 8><<<blocks, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
-    } else if (vec_ok && nvec <= 256 * 4) {
+    } else if (vec_ok && nvec <= 256 * 8) {
         if (nvec <= 256 * 2) rms_block_kernel<T, 2><<<(int)M, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
-        else rms_block_kernel<T, 4><<<(int)M, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
+        else if (nvec <= 256 * 4) rms_block_kernel<T, 4><<<(int)M, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
+        else rms_block_kernel<T, 8><<<(int)M, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
     } else {
         int blocks = (int)(M < (size_t)grid_cap ? M : grid_cap);
         rms_generic_kernel<T><<<blocks, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
