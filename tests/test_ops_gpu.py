@@ -237,6 +237,27 @@ def test_linear_tensor_core_vs_oracle(oracle, cuda):
     np.testing.assert_allclose(as_f32(h(out)), as_f32(want), rtol=2e-2, atol=1e-2)
 
 
+def test_ops_first_use_in_fresh_process(cuda):
+    """Every op works as the first library call of a process (kernel
+    attributes such as shared-memory limits are set on first use, not only
+    by model creation)."""
+    import subprocess
+    import sys
+    code = (
+        "import torch\n"
+        "from wginfer_b200 import ops\n"
+        "bf = torch.bfloat16\n"
+        "for M, N, K in ((1, 2048, 1536), (4, 1536, 8960), (20, 256, 1536)):\n"
+        "    x = torch.randn(M, K, device='cuda').to(bf); w = torch.randn(N, K, device='cuda').to(bf) * 0.02\n"
+        "    o = torch.empty(M, N, device='cuda', dtype=bf); ops.linear(o, x, w)\n"
+        "    torch.testing.assert_close(o.float(), (x.float() @ w.float().T).to(bf).float(), rtol=2e-2, atol=1e-2)\n"
+        "q = torch.randn(1, 12, 128, device='cuda').to(bf); k = torch.randn(700, 2, 128, device='cuda').to(bf)\n"
+        "a = torch.empty_like(q); ops.self_attention(a, q, k, k.clone(), 0.088)\n"
+        "torch.cuda.synchronize(); print('ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+
+
 def test_attention_workspace_contract(cuda):
     """FAST needs no workspace (the cluster folds its key slices in shared
     memory); REFERENCE keeps one score per key in the workspace once the cache
