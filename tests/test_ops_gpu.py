@@ -258,6 +258,44 @@ def test_ops_first_use_in_fresh_process(cuda):
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
 
 
+def _attn_ref(q, k, v, scale):
+    """Causal GQA attention in fp32 torch: query i sees keys j <= i + L - S."""
+    S, nh, d = q.shape
+    L, nkvh, dv = v.shape
+    qf, kf, vf = q.float(), k.float(), v.float()
+    out = torch.empty(S, nh, dv, device=q.device)
+    i = torch.arange(S, device=q.device)[:, None]
+    j = torch.arange(L, device=q.device)[None, :]
+    mask = j > i + (L - S)
+    for h in range(nh):
+        kv = h * nkvh // nh
+        sc = (qf[:, h] @ kf[:, kv].T) * scale
+        sc = sc.masked_fill(mask, float("-inf"))
+        out[:, h] = torch.softmax(sc, -1) @ vf[:, kv]
+    return out
+
+
+# Prefill shapes take the tensor-core kernel (bf16/f16, head dim 64/128, at
+# least 2 x SMs query rows x heads): full causal, causal behind a cached
+# prefix (L > S), ragged query tiles, GQA groups of 6 and 2.
+PREFILL = [(512, 512, 12, 2, 128), (100, 612, 12, 2, 128), (2048, 2048, 12, 2, 128), (333, 333, 8, 4, 64),
+           (64, 1000, 16, 2, 128), (257, 300, 12, 12, 64)]
+
+
+@pytest.mark.parametrize("S,L,nh,nkvh,d", PREFILL)
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_attention_prefill_vs_torch(cuda, S, L, nh, nkvh, d, dt):
+    g = torch.Generator("cpu").manual_seed(S * 7 + L)
+    q = torch.randn(S, nh, d, generator=g).to(dt).cuda()
+    k = torch.randn(L, nkvh, d, generator=g).to(dt).cuda()
+    v = torch.randn(L, nkvh, d, generator=g).to(dt).cuda()
+    out = torch.full((S, nh, d), float("nan"), dtype=dt, device="cuda")
+    scale = 1.0 / d ** 0.5
+    with numerics("fast"):
+        ops.self_attention(out, q, k, v, scale)
+    torch.testing.assert_close(out.float(), _attn_ref(q, k, v, scale), rtol=2e-2, atol=1e-2)
+
+
 def test_attention_workspace_contract(cuda):
     """FAST needs no workspace (the cluster folds its key slices in shared
     memory); REFERENCE keeps one score per key in the workspace once the cache

@@ -22,6 +22,8 @@
 #include <cuda_pipeline.h>
 #include <float.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace cg = cooperative_groups;
@@ -517,6 +519,240 @@ int launch_warp_attn(T *out, const T *q, Src src, const AttnShape &sh, cudaStrea
     return check_launch("self_attention(warp)");
 }
 
+// ---- FAST prefill: query tiles on the tensor cores --------------------------
+// One CTA = 64 consecutive query rows of one head (4 warps x 16 rows). K and V
+// tiles of 64 keys stream through shared memory (cp.async, double-buffered,
+// rows padded by 16 bytes so ldmatrix is free of bank conflicts). Each warp
+// computes S = Q K^T for its 16 rows with mma.sync m16n8k16 (bf16/f16 in, f32
+// accumulate), applies the causal mask (key j visible to query i when
+// j <= i + L - S), folds the tile into a running max and sum (exp2 of scaled
+// scores), and accumulates O += P V with P re-packed from the score
+// registers as the A operand. Rows are normalised once at the end.
+// Roofline at a 512-token prefill: tensor, 4*S*L*d*nh (causal: about half)
+// flops; the K/V bytes are re-read from L2 by each query tile.
+constexpr int kMQ = 64;       // query rows per CTA
+constexpr int kMK = 64;       // keys per tile
+constexpr int kMThreads = 128;
+
+__device__ __forceinline__ uint32_t sm_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void ldsm4(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(sm_u32(p)));
+}
+__device__ __forceinline__ void ldsm4_t(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(sm_u32(p)));
+}
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+}
+template <typename T> __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<uint32_t *>(&v);
+    } else {
+        __half2 v = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t *>(&v);
+    }
+}
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <typename T, int DH> constexpr size_t mma_smem_bytes() {
+    return (size_t)(kMQ + 4 * kMK) * (DH + 8) * sizeof(T);
+}
+
+template <typename T, int DH>
+__global__ void __launch_bounds__(kMThreads) attn_mma_kernel(const T *__restrict__ q, KvDense<T> src,
+                                                             T *__restrict__ out, AttnShape sh) {
+    constexpr int RS = DH + 8;       // shared row stride (elements): 16-byte pad
+    constexpr int CPR = DH / 8;      // 16-byte chunks per row
+    constexpr int NKS = DH / 16;     // k-steps over the head dimension
+    constexpr int NDT = DH / 8;      // 8-wide output column tiles
+    extern __shared__ __align__(16) unsigned char smem[];
+    T *qs = reinterpret_cast<T *>(smem);   // [kMQ][RS]
+    T *ks = qs + kMQ * RS;                 // [2][kMK][RS]
+    T *vs = ks + 2 * kMK * RS;             // [2][kMK][RS]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+    const int q0 = blockIdx.x * kMQ, h = blockIdx.y;
+    const int kvh = h * sh.nkvh / sh.nh;
+    const int off = sh.L - sh.S;  // >= 0: the launcher sends L < S elsewhere
+    const size_t kst = (size_t)sh.nkvh * DH;
+    const T *kb = src.k + (size_t)kvh * DH, *vb = src.v + (size_t)kvh * DH;
+    const int qn = min(kMQ, sh.S - q0);
+    const int kend = min(sh.L, q0 + qn + off);  // keys [0, kend) are visible to some row of the tile
+    const int ntiles = (kend + kMK - 1) / kMK;
+
+    for (int c = tid; c < kMQ * CPR; c += kMThreads) {
+        const int r = c / CPR, cc = c - r * CPR;
+        T *dst = qs + r * RS + cc * 8;
+        if (r < qn) __pipeline_memcpy_async(dst, q + ((size_t)(q0 + r) * sh.nh + h) * DH + cc * 8, 16);
+        else *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+    }
+    auto load_kv = [&](int tile) {
+        if (tile < ntiles) {
+            T *kd = ks + (tile & 1) * kMK * RS, *vd = vs + (tile & 1) * kMK * RS;
+            for (int c = tid; c < kMK * CPR; c += kMThreads) {
+                const int r = c / CPR, cc = c - r * CPR, j = tile * kMK + r;
+                if (j < kend) {
+                    __pipeline_memcpy_async(kd + r * RS + cc * 8, kb + (size_t)j * kst + cc * 8, 16);
+                    __pipeline_memcpy_async(vd + r * RS + cc * 8, vb + (size_t)j * kst + cc * 8, 16);
+                } else {
+                    *reinterpret_cast<uint4 *>(kd + r * RS + cc * 8) = make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4 *>(vd + r * RS + cc * 8) = make_uint4(0, 0, 0, 0);
+                }
+            }
+        }
+        __pipeline_commit();
+    };
+    load_kv(0);  // one group: the Q tile and key tile 0
+    load_kv(1);
+
+    const float sc2 = sh.scale * 1.4426950408889634f;  // scores in log2 units
+    const int qa = q0 + warp * 16 + g, qb = qa + 8;     // this thread's two query rows
+    uint32_t qf[NKS][4];
+    float o[NDT][4];
+#pragma unroll
+    for (int i = 0; i < NDT; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+    for (int tile = 0; tile < ntiles; tile++) {
+        __pipeline_wait_prior(1);
+        __syncthreads();
+        if (tile == 0) {
+#pragma unroll
+            for (int k = 0; k < NKS; k++)
+                ldsm4(qf[k], qs + (warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * RS + k * 16 + (lane >> 4) * 8);
+        }
+        const T *kt = ks + (tile & 1) * kMK * RS, *vt = vs + (tile & 1) * kMK * RS;
+        float s[8][4];
+#pragma unroll
+        for (int n = 0; n < 8; n++) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+        for (int k = 0; k < NKS; k++) {
+#pragma unroll
+            for (int n = 0; n < 8; n += 2) {
+                uint32_t b[4];
+                ldsm4(b, kt + (n * 8 + (lane & 7) + (lane >> 4) * 8) * RS + k * 16 + ((lane >> 3) & 1) * 8);
+                mma16816<T>(s[n], qf[k], b[0], b[1]);
+                mma16816<T>(s[n + 1], qf[k], b[2], b[3]);
+            }
+        }
+        // scale, mask, running max per row (the 4 lanes of a quad share a row)
+        const int j0 = tile * kMK;
+        const bool edge = j0 + kMK > min(q0 + off + 1, kend);  // some key of this tile is masked for some row
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int n = 0; n < 8; n++) {
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float v = s[n][c] * sc2;
+                if (edge) {
+                    const int j = j0 + n * 8 + 2 * t4 + (c & 1);
+                    const int row = c < 2 ? qa : qb;
+                    if (j >= kend || j > row + off) v = -INFINITY;
+                }
+                s[n][c] = v;
+                mx[c >> 1] = fmaxf(mx[c >> 1], v);
+            }
+        }
+        float corr[2];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+            const float mnew = fmaxf(mrow[r], mx[r]);
+            corr[r] = mnew == -INFINITY ? 1.f : ex2(mrow[r] - mnew);
+            mrow[r] = mnew;
+            lrow[r] *= corr[r];
+        }
+#pragma unroll
+        for (int i = 0; i < NDT; i++) {
+            o[i][0] *= corr[0];
+            o[i][1] *= corr[0];
+            o[i][2] *= corr[1];
+            o[i][3] *= corr[1];
+        }
+#pragma unroll
+        for (int n = 0; n < 8; n++) {
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const float m = mrow[c >> 1];
+                const float p = m == -INFINITY ? 0.f : ex2(s[n][c] - m);
+                s[n][c] = p;
+                lrow[c >> 1] += p;
+            }
+        }
+        // O += P V: P (16 x 64) from the score registers, V via transposed ldmatrix
+#pragma unroll
+        for (int kk = 0; kk < kMK / 16; kk++) {
+            uint32_t pa[4];
+            pa[0] = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
+            pa[1] = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
+            pa[2] = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+            pa[3] = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+            for (int nd = 0; nd < NDT; nd += 2) {
+                uint32_t b[4];
+                ldsm4_t(b, vt + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * RS + nd * 8 + (lane >> 4) * 8);
+                mma16816<T>(o[nd], pa, b[0], b[1]);
+                mma16816<T>(o[nd + 1], pa, b[2], b[3]);
+            }
+        }
+        __syncthreads();  // every warp is done with this buffer
+        load_kv(tile + 2);
+    }
+    __pipeline_wait_prior(0);
+    // row sums over the quad, then normalise and store
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+        lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
+    }
+    const float inv0 = lrow[0] > 0.f ? 1.f / lrow[0] : 0.f, inv1 = lrow[1] > 0.f ? 1.f / lrow[1] : 0.f;
+#pragma unroll
+    for (int nd = 0; nd < NDT; nd++) {
+        const int col = nd * 8 + 2 * t4;
+        if (qa < sh.S)
+            *reinterpret_cast<uint32_t *>(out + ((size_t)qa * sh.nh + h) * DH + col) =
+                pack2<T>(o[nd][0] * inv0, o[nd][1] * inv0);
+        if (qb < sh.S)
+            *reinterpret_cast<uint32_t *>(out + ((size_t)qb * sh.nh + h) * DH + col) =
+                pack2<T>(o[nd][2] * inv1, o[nd][3] * inv1);
+    }
+}
+
+template <typename T, int DH>
+int launch_mma_attn(T *out, const T *q, KvDense<T> src, const AttnShape &sh, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((sh.S + kMQ - 1) / kMQ), (unsigned)sh.nh, 1);
+    cfg.blockDim = dim3(kMThreads, 1, 1);
+    cfg.dynamicSmemBytes = mma_smem_bytes<T, DH>();
+    cfg.stream = s;
+    cfg.numAttrs = 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_mma_kernel<T, DH>, q, src, out, sh);
+    if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "self_attention(mma): %s", cudaGetErrorString(e));
+    return check_launch("self_attention(mma)");
+}
+
 // ---- REFERENCE order --------------------------------------------------------
 template <typename T, class Src, bool kVec>
 __global__ void __launch_bounds__(kThreads) attn_ref_kernel(const T *__restrict__ q, Src src, T *__restrict__ out,
@@ -664,6 +900,12 @@ template <typename T, class Src> void set_attrs() {
     cudaFuncSetAttribute(attn_ref_kernel<T, Src, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     cudaFuncSetAttribute(attn_fast_kernel<T, Src, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaFuncSetAttribute(attn_fast_kernel<T, Src, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if constexpr (sizeof(T) == 2) {
+        cudaFuncSetAttribute(attn_mma_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)mma_smem_bytes<T, 128>());
+        cudaFuncSetAttribute(attn_mma_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)mma_smem_bytes<T, 64>());
+    }
     cudaFuncSetAttribute(attn_warp_kernel<T, 128, Src>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)warp_attn_smem<T, 128>());
     cudaFuncSetAttribute(attn_warp_kernel<T, 64, Src>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -706,6 +948,11 @@ int launch_attn(T *out, const T *q, Src src, const AttnShape &sh, bool ref, void
         // few query rows: one head per warp-group, no block barriers in the key loop
         return sh.d == 128 ? launch_warp_attn<T, 128, Src>(out, q, src, sh, s, pf_ptr, pf_bytes)
                            : launch_warp_attn<T, 64, Src>(out, q, src, sh, s, pf_ptr, pf_bytes);
+    }
+    if constexpr (sizeof(T) == 2 && !IsKvCache<Src>::value) {
+        if (vec && sh.d == sh.dv && (sh.d == 128 || sh.d == 64) && sh.L >= sh.S)
+            return sh.d == 128 ? launch_mma_attn<T, 128>(out, q, src, sh, s)
+                               : launch_mma_attn<T, 64>(out, q, src, sh, s);
     }
     const FastSmem lay = fast_smem(sh, sizeof(T));
     cudaLaunchConfig_t cfg = {};
