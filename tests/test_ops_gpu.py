@@ -206,7 +206,8 @@ def test_linear_unaligned_and_ragged(oracle, cuda, mode):
 # rows), N not a multiple of the 128-row weight tile, odd N, K below one
 # 64-wide slice and K not a multiple of it (zero-filled by the copy engine).
 TC_SHAPES = [(9, 128, 64), (20, 256, 1536), (64, 1536, 1536), (64, 17920, 1536), (100, 1536, 8960),
-             (512, 2048, 1536), (200, 37, 104), (33, 300, 24), (1000, 96, 200)]
+             (512, 2048, 1536), (200, 37, 104), (33, 300, 24), (1000, 96, 200), (300, 17920, 1536),
+             (512, 17920, 1536)]
 
 
 @pytest.mark.parametrize("M,N,K", TC_SHAPES)

@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(kThreads) attn_fast_kernel(const T *__restrict
 // so K and V of a chunk arrive in one round trip. The warp folds the chunk
 // into its running (max, sum, output) with shuffles; for P.V each lane owns
 // DH/32 output columns and reads the V rows from shared memory. Warps of a
-// CTA take interleaved chunks of the CTA's key slice; the 8 warps, then the
+// CTA take interleaved chunks of the CTA's key slice; the NW warps, then the
 // cluster's CTAs, are folded in shared memory (pushed into CTA 0).
 //
 // Over a KV cache (kPre) every row but the newest was written by an earlier
@@ -339,19 +339,19 @@ constexpr int kWarpKeys = 32;
 template <class Src> struct IsKvCache { static constexpr bool value = false; };
 template <typename T> struct IsKvCache<KvCache<T>> { static constexpr bool value = true; };
 
-template <typename T, int DH> constexpr size_t warp_attn_smem() { return (size_t)8 * kWarpKeys * DH * sizeof(T); }
+template <typename T, int DH, int NW> constexpr size_t warp_attn_smem() { return (size_t)NW * kWarpKeys * DH * sizeof(T); }
 
-template <typename T, int DH, class Src>
-__global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict__ q, Src src, T *__restrict__ out, AttnShape sh,
+template <typename T, int DH, class Src, int NW>
+__global__ void __launch_bounds__(NW * 32) attn_warp_kernel(const T *__restrict__ q, Src src, T *__restrict__ out, AttnShape sh,
                                                              const void *pf_ptr, size_t pf_bytes) {
     constexpr bool kPre = IsKvCache<Src>::value;
     constexpr int V = 16 / sizeof(T);        // elements per 16-byte vector
     constexpr int NV = DH / V;                // vectors per row
     constexpr int CPL = DH / 32;              // output columns per lane
-    extern __shared__ __align__(16) unsigned char vsm[];  // [8 warps][32 keys][DH] V rows
+    extern __shared__ __align__(16) unsigned char vsm[];  // [NW warps][32 keys][DH] V rows
     __shared__ __align__(16) float qs[DH];
-    __shared__ float wm[8], wl[8];
-    __shared__ __align__(16) float wo[8][DH];
+    __shared__ float wm[NW], wl[NW];
+    __shared__ __align__(16) float wo[NW][DH];
     __shared__ float xm[kMaxCluster], xl[kMaxCluster];
     __shared__ __align__(16) float xo[kMaxCluster][DH];
 
@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict
     pdl_trigger();
     pdl_wait();  // q and the newest cache row are written by the previous kernel
     if (first < c1 && (!kPre || first * kWarpKeys + lane == newest)) fetch(first);
-    for (int c = threadIdx.x; c < DH; c += kThreads) qs[c] = ldf(q, ((size_t)i * sh.nh + h) * DH + c);
+    for (int c = threadIdx.x; c < DH; c += NW * 32) qs[c] = ldf(q, ((size_t)i * sh.nh + h) * DH + c);
     __syncthreads();
 
     float m = -FLT_MAX, l = 0.f;
@@ -402,7 +402,7 @@ __global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict
 #pragma unroll
     for (int c = 0; c < CPL; c++) o[c] = 0.f;
 
-    for (int ch = first; ch < c1; ch += 8) {
+    for (int ch = first; ch < c1; ch += NW) {
         if (ch != first) fetch(ch);
         const int j = ch * kWarpKeys + lane;
         const bool ok = j < nvis;
@@ -449,7 +449,7 @@ __global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict
         }
         __syncwarp();  // the warp's V buffer is refilled by the next chunk
     }
-    // fold the 8 warps
+    // fold the NW warps
     if (lane == 0) {
         wm[warp] = m;
         wl[warp] = l;
@@ -459,15 +459,15 @@ __global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict
     __syncthreads();
     float M = -FLT_MAX;
 #pragma unroll
-    for (int w = 0; w < 8; w++) M = fmaxf(M, wm[w]);
+    for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w]);
     float Lsum = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; w++) Lsum += wl[w] > 0.f ? wl[w] * __expf(wm[w] - M) : 0.f;
+    for (int w = 0; w < NW; w++) Lsum += wl[w] > 0.f ? wl[w] * __expf(wm[w] - M) : 0.f;
     // one column per thread (DH <= 256 threads); push the CTA's slice to CTA 0
     float oc = 0.f;
     if (threadIdx.x < DH) {
 #pragma unroll
-        for (int w = 0; w < 8; w++)
+        for (int w = 0; w < NW; w++)
             if (wl[w] > 0.f) oc += wo[w][threadIdx.x] * __expf(wm[w] - M);
         cluster.map_shared_rank(&xo[0][0], 0)[rank * DH + threadIdx.x] = oc;
     }
@@ -490,20 +490,13 @@ __global__ void __launch_bounds__(kThreads) attn_warp_kernel(const T *__restrict
     }
 }
 
-template <typename T, int DH, class Src>
-int launch_warp_attn(T *out, const T *q, Src src, const AttnShape &sh, cudaStream_t s, const void *pf_ptr,
-                     size_t pf_bytes) {
-    // slices: at most 3 chunks of 32 keys per CTA, so that a head's work is
-    // spread over up to 8 SMs (the per-warp dot and P.V are latency-bound;
-    // fewer busy warps per SM finish them sooner)
-    const int chunks = (sh.L + kWarpKeys - 1) / kWarpKeys;
-    int ns = (chunks + 2) / 3;
-    if (ns > kMaxCluster) ns = kMaxCluster;
-    if (ns < 1) ns = 1;
+template <typename T, int DH, class Src, int NW>
+int launch_warp_attn_nw(T *out, const T *q, Src src, const AttnShape &sh, int ns, cudaStream_t s, const void *pf_ptr,
+                        size_t pf_bytes) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ns, (unsigned)(sh.S * sh.nh), 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = warp_attn_smem<T, DH>();
+    cfg.blockDim = dim3(NW * 32, 1, 1);
+    cfg.dynamicSmemBytes = warp_attn_smem<T, DH, NW>();
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -514,9 +507,23 @@ int launch_warp_attn(T *out, const T *q, Src src, const AttnShape &sh, cudaStrea
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_warp_kernel<T, DH, Src>, q, src, out, sh, pf_ptr, pf_bytes);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_warp_kernel<T, DH, Src, NW>, q, src, out, sh, pf_ptr, pf_bytes);
     if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "self_attention(warp): %s", cudaGetErrorString(e));
     return check_launch("self_attention(warp)");
+}
+
+template <typename T, int DH, class Src>
+int launch_warp_attn(T *out, const T *q, Src src, const AttnShape &sh, cudaStream_t s, const void *pf_ptr,
+                     size_t pf_bytes) {
+    // slices: at most 3 chunks of 32 keys per CTA, so that a head's work is
+    // spread over up to 8 SMs (the per-warp dot and P.V are latency-bound;
+    // fewer busy warps per SM finish them sooner). CTAs of 4 warps (smaller,
+    // to start beside the q/k/v projection) were measured slower.
+    const int chunks = (sh.L + kWarpKeys - 1) / kWarpKeys;
+    int ns = (chunks + 2) / 3;
+    if (ns > kMaxCluster) ns = kMaxCluster;
+    if (ns < 1) ns = 1;
+    return launch_warp_attn_nw<T, DH, Src, 8>(out, q, src, sh, ns, s, pf_ptr, pf_bytes);
 }
 
 // ---- FAST prefill: query tiles on the tensor cores --------------------------
@@ -906,10 +913,10 @@ template <typename T, class Src> void set_attrs() {
         cudaFuncSetAttribute(attn_mma_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)mma_smem_bytes<T, 64>());
     }
-    cudaFuncSetAttribute(attn_warp_kernel<T, 128, Src>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)warp_attn_smem<T, 128>());
-    cudaFuncSetAttribute(attn_warp_kernel<T, 64, Src>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)warp_attn_smem<T, 64>());
+    cudaFuncSetAttribute(attn_warp_kernel<T, 128, Src, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)warp_attn_smem<T, 128, 8>());
+    cudaFuncSetAttribute(attn_warp_kernel<T, 64, Src, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)warp_attn_smem<T, 64, 8>());
 }
 
 void init_attrs_once() {

@@ -21,6 +21,42 @@ __device__ __forceinline__ void row_map(const DecodeGemvParams &p, int g, int &r
     r1 = 2 * g + 1;
 }
 
+// Rows per row pair g of the fused q/k/v projection: g < P = (nh + nkvh) *
+// dh/2 is the rotation pair (j, j + dh/2) of one q or k head, rotated with
+// cs = {cos, sin}(pos, j) and written to q_rope or into the K cache; the
+// other pairs are two consecutive v values for the V cache. pos and cs may be
+// loaded early by the caller (they do not depend on the previous kernel).
+template <typename T>
+__device__ __forceinline__ void rope_kv_store(const DecodeGemvParams &p, int g, bool r1ok, int m, float s0, float s1,
+                                              int64_t pos, float2 cs) {
+    {
+        if (pos < 0 || pos >= p.maxseq) {
+            record_device_error(p.err, 3, pos);
+            return;
+        }
+        const int seq = p.prefill_seq >= 0 ? p.prefill_seq : m;
+        const int half = p.dh >> 1;
+        const int P = (p.nh + p.nkvh) * half;
+        T *kc = reinterpret_cast<T *>(p.kc) + (size_t)seq * p.seq_stride + (size_t)pos * p.nkvh * p.dh;
+        T *vc = reinterpret_cast<T *>(p.vc) + (size_t)seq * p.seq_stride + (size_t)pos * p.nkvh * p.dh;
+        const float a = Elem<T>::load(Elem<T>::store(s0));
+        const float b = Elem<T>::load(Elem<T>::store(s1));
+        if (g < P) {
+            const int h = g / half, j = g - h * half;
+            const float o0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+            const float o1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+            T *dst = h < p.nh ? reinterpret_cast<T *>(p.q_out) + ((size_t)m * p.nh + h) * p.dh
+                              : kc + (size_t)(h - p.nh) * p.dh;
+            stf(dst, j, o0);
+            stf(dst, j + half, o1);
+        } else {
+            const int e = 2 * (g - P);
+            stf(vc, e, a);
+            if (r1ok) stf(vc, e + 1, b);
+        }
+    }
+}
+
 template <typename T, int EPI>
 __device__ __forceinline__ void epilogue(const DecodeGemvParams &p, int g, int r0, int r1, bool r1ok, int m, float s0,
                                          float s1) {
@@ -46,32 +82,24 @@ __device__ __forceinline__ void epilogue(const DecodeGemvParams &p, int g, int r
             __fdiv_rn(__fmul_rn(uu, gg), __fadd_rn(1.0f, expf(-gg))));
     } else {
         const int64_t pos = p.pos[m];
-        if (pos < 0 || pos >= p.maxseq) {
-            record_device_error(p.err, 3, pos);
-            return;
-        }
-        const int seq = p.prefill_seq >= 0 ? p.prefill_seq : m;
         const int half = p.dh >> 1;
         const int P = (p.nh + p.nkvh) * half;
-        T *kc = reinterpret_cast<T *>(p.kc) + (size_t)seq * p.seq_stride + (size_t)pos * p.nkvh * p.dh;
-        T *vc = reinterpret_cast<T *>(p.vc) + (size_t)seq * p.seq_stride + (size_t)pos * p.nkvh * p.dh;
-        const float a = Elem<T>::load(Elem<T>::store(s0));
-        const float b = Elem<T>::load(Elem<T>::store(s1));
-        if (g < P) {
-            const int h = g / half, j = g - h * half;
-            const float2 cs = p.table[(size_t)pos * half + j];
-            const float o0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
-            const float o1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
-            T *dst = h < p.nh ? reinterpret_cast<T *>(p.q_out) + ((size_t)m * p.nh + h) * p.dh
-                              : kc + (size_t)(h - p.nh) * p.dh;
-            stf(dst, j, o0);
-            stf(dst, j + half, o1);
-        } else {
-            const int e = 2 * (g - P);
-            stf(vc, e, a);
-            if (r1ok) stf(vc, e + 1, b);
-        }
+        float2 cs = make_float2(0.f, 0.f);
+        if (g < P && pos >= 0 && pos < p.maxseq) cs = p.table[(size_t)pos * half + (g % half)];
+        rope_kv_store<T>(p, g, r1ok, m, s0, s1, pos, cs);
     }
+}
+
+// The RoPE/KV epilogue with pos and {cos, sin} loaded by the caller.
+template <typename T>
+__device__ __forceinline__ void epilogue_ropekv_pre(const DecodeGemvParams &p, int g, int r0, int r1, bool r1ok, int m,
+                                                    float s0, float s1, int64_t pos, float2 cs) {
+    const T *bias = reinterpret_cast<const T *>(p.bias);
+    if (bias) {
+        s0 += ldf(bias, r0);
+        if (r1ok) s1 += ldf(bias, r1);
+    }
+    rope_kv_store<T>(p, g, r1ok, m, s0, s1, pos, cs);
 }
 
 }  // namespace wgb

@@ -108,6 +108,20 @@ __global__ void __launch_bounds__(256, (MT <= 2 ? 3 : 2)) decode_gemv_kernel(Dec
         l2_prefetch_share(p.pf_ptr[0], p.pf_bytes[0], blockIdx.x, gridDim.x);
         l2_prefetch_share(p.pf_ptr[1], p.pf_bytes[1], blockIdx.x, gridDim.x);
     }
+    // RoPE epilogue: the positions (set at the start of the step) and the
+    // host-built cos/sin table do not depend on the previous kernel; the
+    // epilogue lanes of the first block fetch their entries now.
+    int64_t pos_pre = 0;
+    float2 cs_pre = make_float2(0.f, 0.f);
+    if (EPI == EPI_ROPEKV && ks == 0 && lane < M) {
+        const int g0 = (int)blockIdx.x * GROUPS + rg;
+        if (g0 < p.groups) {
+            pos_pre = p.pos[lane];
+            const int half = p.dh >> 1;
+            if (g0 < (p.nh + p.nkvh) * half && pos_pre >= 0 && pos_pre < p.maxseq)
+                cs_pre = p.table[(size_t)pos_pre * half + (g0 % half)];
+        }
+    }
     pdl_trigger();
     pdl_wait();
     const T *x = reinterpret_cast<const T *>(p.x);
@@ -239,7 +253,10 @@ __global__ void __launch_bounds__(256, (MT <= 2 ? 3 : 2)) decode_gemv_kernel(Dec
                         s1 = acc[1][mm];
                     }
             }
-            epilogue<T, EPI>(p, g, r0, r1, r1ok, m, s0, s1);
+            if (EPI == EPI_ROPEKV && blk == (int)blockIdx.x)
+                epilogue_ropekv_pre<T>(p, g, r0, r1, r1ok, m, s0, s1, pos_pre, cs_pre);
+            else
+                epilogue<T, EPI>(p, g, r0, r1, r1ok, m, s0, s1);
         }
         if (KS > 1) __syncthreads();  // red[] is rewritten by the next block
     }

@@ -32,7 +32,7 @@ namespace {
 
 constexpr int kTcThreads = 128;
 constexpr int kBK = 64;          // K elements per stage (128 bytes of bf16: one swizzle span)
-constexpr int kTcStages = 4;
+constexpr int kTcMaxStages = 8;
 constexpr int kTileW = 128;      // weight rows per CTA (MMA M)
 constexpr long long kTcWaitCycles = 4000000000ll;  // a stage stalled this long (about 2 s) counts as a failure
 
@@ -105,17 +105,26 @@ __host__ __device__ inline uint32_t idesc_bf16(int tn) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(tn >> 3) << 17) | ((uint32_t)(kTileW >> 4) << 24);
 }
 
+// Stages in the ring: 4. Deeper rings for the narrow tiles were measured
+// slower: their shared memory halves the CTAs resident per SM, and a CTA's
+// throughput does not grow with its ring depth.
+inline int tc_stages(int) { return 4; }
 inline size_t tc_smem_bytes(int tn) {
-    return 1024 + (size_t)kTcStages * ((size_t)kTileW * kBK * 2 + (size_t)tn * kBK * 2);
+    return 1024 + (size_t)tc_stages(tn) * ((size_t)kTileW * kBK * 2 + (size_t)tn * kBK * 2);
+}
+inline size_t tc_smem_max() {
+    size_t m = 0;
+    for (int tn = 16; tn <= 256; tn *= 2) m = tc_smem_bytes(tn) > m ? tc_smem_bytes(tn) : m;
+    return m;
 }
 
 template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, DecodeGemvParams p,
-                   int tn) {
+                   int tn, int nst) {
     using T = __nv_bfloat16;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done;
+    __shared__ __align__(8) uint64_t full[kTcMaxStages], empty[kTcMaxStages], done;
     __shared__ uint32_t s_tmem;
     __shared__ int s_bad, s_issued;
     unsigned char *smem = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -128,7 +137,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (threadIdx.x == 0) {
         s_bad = 0;
         s_issued = 0;
-        for (int i = 0; i < kTcStages; i++) {
+        for (int i = 0; i < nst; i++) {
             mb_init(&full[i], 1);
             mb_init(&empty[i], 1);
         }
@@ -151,8 +160,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == 0 && lane == 0) {
         // producer: TMA slices of W (128 rows) and X (tn rows) into the ring
         for (int kt = 0; kt < ktiles; kt++) {
-            const int st = kt % kTcStages;
-            if (kt >= kTcStages && !mb_wait(&empty[st], (unsigned)(((kt / kTcStages) - 1) & 1))) {
+            const int st = kt % nst;
+            if (kt >= nst && !mb_wait(&empty[st], (unsigned)(((kt / nst) - 1) & 1))) {
                 atomicExch(&s_bad, 1);
                 break;
             }
@@ -166,8 +175,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // MMA issuer
         const uint32_t idesc = idesc_bf16(tn);
         for (int kt = 0; kt < ktiles; kt++) {
-            const int st = kt % kTcStages;
-            if (!mb_wait(&full[st], (unsigned)((kt / kTcStages) & 1))) {
+            const int st = kt % nst;
+            if (!mb_wait(&full[st], (unsigned)((kt / nst) & 1))) {
                 atomicExch(&s_bad, 1);
                 break;
             }
@@ -204,8 +213,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         record_device_error(p.err, 6, blockIdx.x);
         // TMA copies may still be landing in the ring: wait (bounded) for
         // the last one issued into each stage before the CTA exits
-        for (int kt = s_issued - 1; kt >= 0 && kt >= s_issued - kTcStages; kt--)
-            mb_wait(&full[kt % kTcStages], (unsigned)((kt / kTcStages) & 1));
+        for (int kt = s_issued - 1; kt >= 0 && kt >= s_issued - nst; kt--)
+            mb_wait(&full[kt % nst], (unsigned)((kt / nst) & 1));
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -243,12 +252,13 @@ bool make_map(CUtensorMap *tm, const void *base, int rows, int K, int box_rows) 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Input rows per tile: the smallest power of two >= M up to 128, then halved
-// (down to 16) while the grid would leave SMs idle; each halving re-reads the
-// weights once more, mostly from L2.
+// Input rows per tile: the smallest power of two >= M up to 256 (the MMA's
+// largest N; fewer re-reads of the weight tile), then halved (down to 16)
+// while the grid would leave SMs idle; each halving re-reads the weights once
+// more, mostly from L2.
 int pick_tn(int M, int N) {
     int tn = 16;
-    while (tn < M && tn < 128) tn *= 2;
+    while (tn < M && tn < 256) tn *= 2;
     const long long wtiles = (N + kTileW - 1) / kTileW;
     while (tn > 16 && wtiles * ((M + tn - 1) / tn) < sm_count()) tn /= 2;
     return tn;
@@ -266,7 +276,7 @@ int launch_tc(const DecodeGemvParams &p, cudaStream_t s) {
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
         cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)tc_smem_bytes(256));
+                                             (int)tc_smem_max());
         if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "linear(tc): %s", cudaGetErrorString(e));
         if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
     }
@@ -280,7 +290,7 @@ int launch_tc(const DecodeGemvParams &p, cudaStream_t s) {
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI>, tmW, tmX, p, tn);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI>, tmW, tmX, p, tn, tc_stages(tn));
     if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "linear(tc): %s", cudaGetErrorString(e));
     return WGB_OK;
 }
@@ -302,7 +312,7 @@ int tc_gemm(const DecodeGemvParams &p0, int epi, cudaStream_t s) {
 }
 
 void tc_gemm_prepare() {
-    const int lim = (int)tc_smem_bytes(256);
+    const int lim = (int)tc_smem_max();
     cudaFuncSetAttribute(tc_gemm_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     cudaFuncSetAttribute(tc_gemm_kernel<EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     cudaFuncSetAttribute(tc_gemm_kernel<EPI_ROPEKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
