@@ -760,6 +760,265 @@ int launch_mma_attn(T *out, const T *q, KvDense<T> src, const AttnShape &sh, cud
     return check_launch("self_attention(mma)");
 }
 
+// ---- FAST batched decode: GQA groups on the tensor cores --------------------
+// One CTA = one (sequence, kv head) and one slice of its keys. The hpc query
+// heads that share the kv head are the 16 rows of an m16n8k16 A tile (rows
+// past hpc are zero), so every K/V row is read once per kv head and feeds
+// hpc query heads through mma.sync. Four warps split the CTA's keys; each
+// streams its own 32-key K/V tiles through a double-buffered shared-memory
+// stage (cp.async), keeps a running max/sum per row and O += P V in
+// registers. The warps fold in shared memory, then the CTAs of the cluster
+// (the key slices) fold in CTA 0 through distributed shared memory.
+// Roofline: HBM, 2 * B * L * nkvh * d * size bytes of K/V.
+constexpr int kDW = 4;        // warps per CTA
+constexpr int kDK = 32;       // keys per warp tile
+
+template <typename T, int DH> struct MmaDecLayout {
+    static constexpr int RS = DH + 8;
+    static constexpr size_t tile = (size_t)kDK * RS * sizeof(T);      // one K or V tile
+    static constexpr size_t warp_stage = 4 * tile;                    // K, V x 2 buffers
+    static constexpr size_t qs = 0;                                   // [16][RS] T
+    static constexpr size_t kv = ((size_t)16 * RS * sizeof(T) + 127) & ~(size_t)127;
+    static constexpr size_t xo = kv + kDW * warp_stage;               // rank 0: [ns][16][DH] f32
+    static constexpr size_t bytes(int ns) { return xo + (size_t)ns * 16 * DH * 4; }
+};
+
+template <typename T, int DH>
+__global__ void __launch_bounds__(kDW * 32) attn_mma_decode_kernel(const T *__restrict__ q, KvCache<T> src,
+                                                                   T *__restrict__ out, AttnShape sh) {
+    using Lay = MmaDecLayout<T, DH>;
+    constexpr int RS = Lay::RS, CPR = DH / 8, NKS = DH / 16, NDT = DH / 8;
+    extern __shared__ __align__(128) unsigned char smem[];
+    T *qs = reinterpret_cast<T *>(smem + Lay::qs);
+    float *xo = reinterpret_cast<float *>(smem + Lay::xo);
+    __shared__ float wm[kDW][16], wl[kDW][16];
+    __shared__ float xm[kMaxCluster][16], xl[kMaxCluster][16];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank(), ns = (int)cluster.num_blocks();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+    const int b = blockIdx.y / sh.nkvh, kvh = blockIdx.y % sh.nkvh;
+    const int hpc = sh.nh / sh.nkvh, h0 = kvh * hpc;
+    const T *k, *v;
+    int nkeys, nvis;
+    bool uniform;
+    src.row(sh, b, k, v, nkeys, nvis, uniform);
+    const size_t kst = (size_t)sh.nkvh * DH;
+    const T *kb = k + (size_t)kvh * DH, *vb = v + (size_t)kvh * DH;
+    const int per = (nvis + ns - 1) / ns;
+    const int c0 = min(rank * per, nvis), c1 = min(c0 + per, nvis);
+    const int wper = (c1 - c0 + kDW - 1) / kDW;
+    const int w0 = min(c0 + warp * wper, c1), w1 = min(w0 + wper, c1);
+    const int ntiles = (w1 - w0 + kDK - 1) / kDK;
+    T *kbuf = reinterpret_cast<T *>(smem + Lay::kv + (size_t)warp * Lay::warp_stage);  // [2][kDK][RS]
+    T *vbuf = kbuf + 2 * kDK * RS;                                                     // [2][kDK][RS]
+    auto load_tile = [&](int t) {  // this warp's tile t
+        if (t < ntiles) {
+            T *kd = kbuf + (t & 1) * kDK * RS, *vd = vbuf + (t & 1) * kDK * RS;
+            for (int c = lane; c < kDK * CPR; c += 32) {
+                const int r = c / CPR, cc = c - r * CPR, j = w0 + t * kDK + r;
+                if (j < w1) {
+                    __pipeline_memcpy_async(kd + r * RS + cc * 8, kb + (size_t)j * kst + cc * 8, 16);
+                    __pipeline_memcpy_async(vd + r * RS + cc * 8, vb + (size_t)j * kst + cc * 8, 16);
+                } else {
+                    *reinterpret_cast<uint4 *>(kd + r * RS + cc * 8) = make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4 *>(vd + r * RS + cc * 8) = make_uint4(0, 0, 0, 0);
+                }
+            }
+        }
+        __pipeline_commit();
+    };
+    pdl_trigger();
+    pdl_wait();  // q and the newest cache rows come from the previous kernel
+    for (int c = tid; c < 16 * CPR; c += kDW * 32) {
+        const int r = c / CPR, cc = c - r * CPR;
+        T *dst = qs + r * RS + cc * 8;
+        if (r < hpc) __pipeline_memcpy_async(dst, q + ((size_t)b * sh.nh + h0 + r) * DH + cc * 8, 16);
+        else *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+    }
+    __pipeline_commit();
+    load_tile(0);
+    load_tile(1);
+    __pipeline_wait_prior(2);
+    __syncthreads();  // the Q tile is shared by the four warps
+    uint32_t qf[NKS][4];
+#pragma unroll
+    for (int kk = 0; kk < NKS; kk++)
+        ldsm4(qf[kk], qs + ((lane & 7) + ((lane >> 3) & 1) * 8) * RS + kk * 16 + (lane >> 4) * 8);
+    const float sc2 = sh.scale * 1.4426950408889634f;
+    float o[NDT][4];
+#pragma unroll
+    for (int i = 0; i < NDT; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+    for (int t = 0; t < ntiles; t++) {
+        __pipeline_wait_prior(1);
+        __syncwarp();
+        const T *kt = kbuf + (t & 1) * kDK * RS, *vt = vbuf + (t & 1) * kDK * RS;
+        float s[4][4];
+#pragma unroll
+        for (int n = 0; n < 4; n++) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < NKS; kk++) {
+#pragma unroll
+            for (int n = 0; n < 4; n += 2) {
+                uint32_t bb[4];
+                ldsm4(bb, kt + (n * 8 + (lane & 7) + (lane >> 4) * 8) * RS + kk * 16 + ((lane >> 3) & 1) * 8);
+                mma16816<T>(s[n], qf[kk], bb[0], bb[1]);
+                mma16816<T>(s[n + 1], qf[kk], bb[2], bb[3]);
+            }
+        }
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int n = 0; n < 4; n++) {
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const int j = w0 + t * kDK + n * 8 + 2 * t4 + (c & 1);
+                const float val = j < w1 ? (uniform ? 0.f : s[n][c] * sc2) : -INFINITY;
+                s[n][c] = val;
+                mx[c >> 1] = fmaxf(mx[c >> 1], val);
+            }
+        }
+        float corr[2];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+            const float mnew = fmaxf(mrow[r], mx[r]);
+            corr[r] = mnew == -INFINITY ? 1.f : ex2(mrow[r] - mnew);
+            mrow[r] = mnew;
+            lrow[r] *= corr[r];
+        }
+#pragma unroll
+        for (int i = 0; i < NDT; i++) {
+            o[i][0] *= corr[0];
+            o[i][1] *= corr[0];
+            o[i][2] *= corr[1];
+            o[i][3] *= corr[1];
+        }
+#pragma unroll
+        for (int n = 0; n < 4; n++) {
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const float m = mrow[c >> 1];
+                const float p = m == -INFINITY ? 0.f : ex2(s[n][c] - m);
+                s[n][c] = p;
+                lrow[c >> 1] += p;
+            }
+        }
+#pragma unroll
+        for (int kk = 0; kk < kDK / 16; kk++) {
+            uint32_t pa[4];
+            pa[0] = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
+            pa[1] = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
+            pa[2] = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+            pa[3] = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+            for (int nd = 0; nd < NDT; nd += 2) {
+                uint32_t bb[4];
+                ldsm4_t(bb, vt + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * RS + nd * 8 + (lane >> 4) * 8);
+                mma16816<T>(o[nd], pa, bb[0], bb[1]);
+                mma16816<T>(o[nd + 1], pa, bb[2], bb[3]);
+            }
+        }
+        __syncwarp();  // this buffer is refilled next
+        load_tile(t + 2);
+    }
+    __pipeline_wait_prior(0);
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+        lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
+    }
+    if (t4 == 0) {
+        wm[warp][g] = mrow[0];
+        wm[warp][g + 8] = mrow[1];
+        wl[warp][g] = lrow[0];
+        wl[warp][g + 8] = lrow[1];
+    }
+    // this warp's unnormalised rows, [16][DH] f32, into its idle stage
+    float *ow = reinterpret_cast<float *>(kbuf);
+#pragma unroll
+    for (int nd = 0; nd < NDT; nd++) {
+        const int col = nd * 8 + 2 * t4;
+        ow[g * DH + col] = o[nd][0];
+        ow[g * DH + col + 1] = o[nd][1];
+        ow[(g + 8) * DH + col] = o[nd][2];
+        ow[(g + 8) * DH + col + 1] = o[nd][3];
+    }
+    __syncthreads();
+    // fold the warps into this CTA's slice and push it to CTA 0 of the cluster
+    float *xo0 = cluster.map_shared_rank(xo, 0);
+    float *xm0 = cluster.map_shared_rank(&xm[0][0], 0), *xl0 = cluster.map_shared_rank(&xl[0][0], 0);
+    for (int x = tid; x < 16 * DH; x += kDW * 32) {
+        const int row = x / DH, col = x - row * DH;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kDW; w++) M = fmaxf(M, wm[w][row]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kDW; w++) {
+                if (wl[w][row] > 0.f) {
+                    const float e = ex2(wm[w][row] - M);
+                    L += wl[w][row] * e;
+                    O += reinterpret_cast<const float *>(smem + Lay::kv + (size_t)w * Lay::warp_stage)[row * DH + col] * e;
+                }
+            }
+        }
+        xo0[((size_t)rank * 16 + row) * DH + col] = O;
+        if (col == 0) {
+            xm0[rank * 16 + row] = M;
+            xl0[rank * 16 + row] = L;
+        }
+    }
+    cluster.sync();
+    if (rank == 0) {
+        for (int x = tid; x < hpc * DH; x += kDW * 32) {
+            const int row = x / DH, col = x - row * DH;
+            float MM = -INFINITY;
+            for (int r = 0; r < ns; r++) MM = fmaxf(MM, xm[r][row]);
+            float LL = 0.f, OO = 0.f;
+            if (MM != -INFINITY) {
+                for (int r = 0; r < ns; r++) {
+                    if (xl[r][row] > 0.f) {
+                        const float e = ex2(xm[r][row] - MM);
+                        LL += xl[r][row] * e;
+                        OO += xo[((size_t)r * 16 + row) * DH + col] * e;
+                    }
+                }
+            }
+            stf(out, ((size_t)b * sh.nh + h0 + row) * DH + col, LL > 0.f ? OO / LL : 0.f);
+        }
+    }
+}
+
+template <typename T, int DH>
+int launch_mma_decode(T *out, const T *q, KvCache<T> src, const AttnShape &sh, cudaStream_t s) {
+    // key slices: about 512 keys per CTA at the longest length this launch
+    // serves (the cluster size depends only on it, so a captured graph stays
+    // valid as the caches grow)
+    int ns = (sh.L + 511) / 512;
+    if (ns > kMaxCluster) ns = kMaxCluster;
+    if (ns < 1) ns = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ns, (unsigned)(sh.S * sh.nkvh), 1);
+    cfg.blockDim = dim3(kDW * 32, 1, 1);
+    cfg.dynamicSmemBytes = MmaDecLayout<T, DH>::bytes(ns);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)ns;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_mma_decode_kernel<T, DH>, q, src, out, sh);
+    if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "self_attention(mma decode): %s", cudaGetErrorString(e));
+    return check_launch("self_attention(mma decode)");
+}
+
 // ---- REFERENCE order --------------------------------------------------------
 template <typename T, class Src, bool kVec>
 __global__ void __launch_bounds__(kThreads) attn_ref_kernel(const T *__restrict__ q, Src src, T *__restrict__ out,
@@ -907,6 +1166,12 @@ template <typename T, class Src> void set_attrs() {
     cudaFuncSetAttribute(attn_ref_kernel<T, Src, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     cudaFuncSetAttribute(attn_fast_kernel<T, Src, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaFuncSetAttribute(attn_fast_kernel<T, Src, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if constexpr (sizeof(T) == 2 && IsKvCache<Src>::value) {
+        cudaFuncSetAttribute(attn_mma_decode_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)MmaDecLayout<T, 128>::bytes(kMaxCluster));
+        cudaFuncSetAttribute(attn_mma_decode_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)MmaDecLayout<T, 64>::bytes(kMaxCluster));
+    }
     if constexpr (sizeof(T) == 2) {
         cudaFuncSetAttribute(attn_mma_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)mma_smem_bytes<T, 128>());
@@ -950,6 +1215,13 @@ int launch_attn(T *out, const T *q, Src src, const AttnShape &sh, bool ref, void
         if (vec) attn_ref_kernel<T, Src, true><<<sh.S * sh.nh, kThreads, smem, s>>>(q, src, out, g ? (float *)ws : nullptr, sh);
         else attn_ref_kernel<T, Src, false><<<sh.S * sh.nh, kThreads, smem, s>>>(q, src, out, g ? (float *)ws : nullptr, sh);
         return check_launch("self_attention(reference)");
+    }
+    if constexpr (sizeof(T) == 2 && IsKvCache<Src>::value) {
+        // batched decode: one CTA per (sequence, kv head) and key slice, the
+        // query heads of the group as the rows of a tensor-core tile
+        if (vec && sh.d == sh.dv && (sh.d == 128 || sh.d == 64) && sh.nh / sh.nkvh <= 16 && sh.S * sh.nkvh >= 32)
+            return sh.d == 128 ? launch_mma_decode<T, 128>(out, q, src, sh, s)
+                               : launch_mma_decode<T, 64>(out, q, src, sh, s);
     }
     if (vec && sh.d == sh.dv && (sh.d == 128 || sh.d == 64) && (long)sh.S * sh.nh < 2L * sm_count()) {
         // few query rows: one head per warp-group, no block barriers in the key loop
