@@ -153,3 +153,21 @@ def test_infer_sampling_path(cuda):
     t = m.infer(CS.prompt(8, CS.TINY.voc), top_k=50, top_p=0.9, temperature=0.7)
     assert 0 <= t < CS.TINY.voc
     assert m.cache_len() == 8
+
+
+def test_checkpoint_load_matches_direct_weights(cuda, tmp_path):
+    """A Hugging Face layout checkpoint loaded through wginfer_b200.checkpoint
+    decodes the same greedy stream as the same weights set directly."""
+    from tests.test_checkpoint import write_checkpoint
+    from wginfer_b200 import checkpoint as CK
+    cfg = CS.TINY
+    w = qwen2_weights(cfg, seed=0)
+    write_checkpoint(tmp_path, cfg, w)
+    ids = CS.prompt(9, cfg.voc, seed=2)
+    with numerics("reference"):
+        want = model(cfg).generate(ids, 12, stop_at_eos=False)
+        m = CK.load_qwen2(tmp_path, device=0, maxseq=cfg.maxseq)
+        assert (m.cfg.nlayer, m.cfg.hs, m.cfg.voc) == (cfg.nlayer, cfg.hs, cfg.voc)
+        got = m.generate(ids, 12, stop_at_eos=False)
+        del m
+    assert got == want

@@ -56,6 +56,12 @@ __device__ __forceinline__ uint4 ld_global_nc_v4(const void *p) {
                  : "l"(p));
     return r;
 }
+// Read-only load that allocates in L1 (operands every CTA of an SM re-reads).
+__device__ __forceinline__ uint4 ld_global_l1_v4(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
 // Streaming load for data read exactly once (weights): evict-first in L2,
 // expressed as an L2 cache-policy operand.
 __device__ __forceinline__ uint64_t evict_first_policy() {

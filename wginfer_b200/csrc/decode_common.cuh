@@ -90,16 +90,41 @@ __device__ __forceinline__ void epilogue(const DecodeGemvParams &p, int g, int r
     }
 }
 
-// The RoPE/KV epilogue with pos and {cos, sin} loaded by the caller.
-template <typename T>
-__device__ __forceinline__ void epilogue_ropekv_pre(const DecodeGemvParams &p, int g, int r0, int r1, bool r1ok, int m,
-                                                    float s0, float s1, int64_t pos, float2 cs) {
-    const T *bias = reinterpret_cast<const T *>(p.bias);
-    if (bias) {
-        s0 += ldf(bias, r0);
-        if (r1ok) s1 += ldf(bias, r1);
+// Operands of the epilogue of a CTA's first row block, loaded early by the
+// caller: the bias (before the wait for the previous kernel: it does not
+// depend on it), the residual (right after the wait, so its round trip
+// overlaps the dot products), and for RoPE the position and {cos, sin}.
+struct EpiPre {
+    float b0 = 0.f, b1 = 0.f;  // bias of rows r0, r1 (0 without bias)
+    float q0 = 0.f, q1 = 0.f;  // residual at (m, r0), (m, r1) (STORE with residual)
+    int64_t pos = 0;
+    float2 cs = make_float2(0.f, 0.f);
+};
+
+template <typename T, int EPI>
+__device__ __forceinline__ void epilogue_pre(const DecodeGemvParams &p, int g, int r0, int r1, bool r1ok, int m,
+                                             float s0, float s1, const EpiPre &e) {
+    if (p.bias) {
+        s0 += e.b0;
+        s1 += e.b1;
     }
-    rope_kv_store<T>(p, g, r1ok, m, s0, s1, pos, cs);
+    if (EPI == EPI_STORE) {
+        T *out = reinterpret_cast<T *>(p.out);
+        const size_t i0 = (size_t)m * p.ldo + r0, i1 = (size_t)m * p.ldo + r1;
+        if (p.res) {
+            s0 = __fadd_rn(e.q0, Elem<T>::load(Elem<T>::store(s0)));
+            s1 = __fadd_rn(e.q1, Elem<T>::load(Elem<T>::store(s1)));
+        }
+        stf(out, i0, s0);
+        if (r1ok) stf(out, i1, s1);
+    } else if (EPI == EPI_SWIGLU) {
+        const float gg = Elem<T>::load(Elem<T>::store(s0));
+        const float uu = Elem<T>::load(Elem<T>::store(s1));
+        stf(reinterpret_cast<T *>(p.out), (size_t)m * p.ldo + g,
+            __fdiv_rn(__fmul_rn(uu, gg), __fadd_rn(1.0f, expf(-gg))));
+    } else {
+        rope_kv_store<T>(p, g, r1ok, m, s0, s1, e.pos, e.cs);
+    }
 }
 
 }  // namespace wgb

@@ -27,6 +27,8 @@
 // (griddepcontrol.wait); it allows the next kernel to launch at once
 // (griddepcontrol.launch_dependents), so launches and weight fetches overlap
 // the previous kernel's tail.
+#include <cuda_pipeline.h>
+
 #include <atomic>
 
 #include "common.cuh"
@@ -53,9 +55,11 @@ __global__ void __launch_bounds__(256, (MT <= 2 ? 3 : 2)) decode_gemv_kernel(Dec
     constexpr int GROUPS = 8 / KS;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T *xs = reinterpret_cast<T *>(smem_raw);  // [MT][K] normalised input (PRO_RMS)
+    T *nws = xs + (size_t)MT * p.K;           // [K] norm weight (PRO_RMS)
     __shared__ float red[8][kRows][MT];
     __shared__ float s_scale[MT];
     __shared__ float s_part[8][MT];
+    __shared__ float s_epi[8][MT][4];  // first block: bias (b0, b1) and residual (q0, q1) per warp and row
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rg = warp / KS, ks = warp % KS;
@@ -111,26 +115,51 @@ __global__ void __launch_bounds__(256, (MT <= 2 ? 3 : 2)) decode_gemv_kernel(Dec
     // RoPE epilogue: the positions (set at the start of the step) and the
     // host-built cos/sin table do not depend on the previous kernel; the
     // epilogue lanes of the first block fetch their entries now.
+    // The bias of the first block's rows is fetched now too (parked in shared
+    // memory, not held in registers across the main loop), and the RMS
+    // prologue's norm weight is copied into shared memory (cp.async).
+    const int g_first = (int)blockIdx.x * GROUPS + rg;
+    int r0_first = 0, r1_first = 0;
+    if (g_first < p.groups) row_map<EPI>(p, g_first, r0_first, r1_first);
+    const bool epi_lane = ks == 0 && lane < M && lane < MT && g_first < p.groups;
     int64_t pos_pre = 0;
     float2 cs_pre = make_float2(0.f, 0.f);
-    if (EPI == EPI_ROPEKV && ks == 0 && lane < M) {
-        const int g0 = (int)blockIdx.x * GROUPS + rg;
-        if (g0 < p.groups) {
+    float b0_pre = 0.f, b1_pre = 0.f;
+    if (epi_lane) {
+        if (p.bias) {
+            b0_pre = ldf(reinterpret_cast<const T *>(p.bias), r0_first);
+            if (r1_first < p.N) b1_pre = ldf(reinterpret_cast<const T *>(p.bias), r1_first);
+        }
+        if (EPI == EPI_ROPEKV) {
             pos_pre = p.pos[lane];
             const int half = p.dh >> 1;
-            if (g0 < (p.nh + p.nkvh) * half && pos_pre >= 0 && pos_pre < p.maxseq)
-                cs_pre = p.table[(size_t)pos_pre * half + (g0 % half)];
+            if (g_first < (p.nh + p.nkvh) * half && pos_pre >= 0 && pos_pre < p.maxseq)
+                cs_pre = p.table[(size_t)pos_pre * half + (g_first % half)];
         }
     }
+    if (PRO == PRO_RMS) {
+        for (int vi = threadIdx.x; vi < nvec; vi += 256)
+            __pipeline_memcpy_async(nws + (size_t)vi * V, reinterpret_cast<const T *>(p.norm_w) + (size_t)vi * V, 16);
+        __pipeline_commit();
+    }
     pdl_trigger();
+    if (epi_lane && p.bias) {
+        s_epi[warp][lane][0] = b0_pre;
+        s_epi[warp][lane][1] = b1_pre;
+    }
     pdl_wait();
+    // the residual of the first block's outputs (written by earlier kernels)
+    if (EPI == EPI_STORE && p.res && epi_lane) {
+        const T *res = reinterpret_cast<const T *>(p.res);
+        s_epi[warp][lane][2] = ldf(res, (size_t)lane * p.ldo + r0_first);
+        if (r1_first < p.N) s_epi[warp][lane][3] = ldf(res, (size_t)lane * p.ldo + r1_first);
+    }
     const T *x = reinterpret_cast<const T *>(p.x);
     if (PRO == PRO_RMS) {
         // every (persistent) CTA normalises the few input rows once: one
         // round trip of 16-byte loads (x rows and the norm weight together),
         // raw rows parked in shared memory, a block reduction, then the
         // scaling pass over shared memory
-        const T *nw = reinterpret_cast<const T *>(p.norm_w);
         float ss[MT];
 #pragma unroll
         for (int m = 0; m < MT; m++) ss[m] = 0.f;
@@ -161,10 +190,11 @@ __global__ void __launch_bounds__(256, (MT <= 2 ? 3 : 2)) decode_gemv_kernel(Dec
             const float mean = __fdiv_rn(t, (float)K);
             s_scale[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
         }
+        __pipeline_wait_prior(0);  // this thread's norm-weight copies have landed
         __syncthreads();
         for (int vi = threadIdx.x; vi < nvec; vi += 256) {
             Vec16<T> wv;
-            wv.u = ld_global_nc_v4(nw + (size_t)vi * V);
+            wv.u = *reinterpret_cast<const uint4 *>(nws + (size_t)vi * V);
 #pragma unroll
             for (int m = 0; m < MT; m++) {
                 if (m < M) {
@@ -223,7 +253,14 @@ __global__ void __launch_bounds__(256, (MT <= 2 ? 3 : 2)) decode_gemv_kernel(Dec
                 }
             }
         }
+        // the next block's first chunk is requested now (an L2 hit: it was
+        // prefetched a block ago), so its round trip overlaps this block's
+        // reduction and epilogue
         have = false;
+        if (blk + (int)gridDim.x < nblocks) {
+            load_chunk(blk + gridDim.x, v0);
+            have = true;
+        }
 #pragma unroll
         for (int r = 0; r < kRows; r++)
 #pragma unroll
@@ -253,9 +290,20 @@ __global__ void __launch_bounds__(256, (MT <= 2 ? 3 : 2)) decode_gemv_kernel(Dec
                         s1 = acc[1][mm];
                     }
             }
-            if (EPI == EPI_ROPEKV && blk == (int)blockIdx.x)
-                epilogue_ropekv_pre<T>(p, g, r0, r1, r1ok, m, s0, s1, pos_pre, cs_pre);
-            else
+            if (blk == (int)blockIdx.x) {
+                EpiPre pre;
+                if (p.bias) {
+                    pre.b0 = s_epi[warp][m][0];
+                    pre.b1 = s_epi[warp][m][1];
+                }
+                if (EPI == EPI_STORE && p.res) {
+                    pre.q0 = s_epi[warp][m][2];
+                    pre.q1 = r1ok ? s_epi[warp][m][3] : 0.f;
+                }
+                pre.pos = pos_pre;
+                pre.cs = cs_pre;
+                epilogue_pre<T, EPI>(p, g, r0, r1, r1ok, m, s0, s1, pre);
+            } else
                 epilogue<T, EPI>(p, g, r0, r1, r1ok, m, s0, s1);
         }
         if (KS > 1) __syncthreads();  // red[] is rewritten by the next block
@@ -291,7 +339,7 @@ template <typename T, int MT, int KS, int PRO, int EPI>
 int launch_one(const DecodeGemvParams &p, cudaStream_t s) {
     constexpr int GROUPS = 8 / KS;
     const int nblocks = (p.groups + GROUPS - 1) / GROUPS;
-    const size_t smem = PRO == PRO_RMS ? (size_t)MT * p.K * sizeof(T) : 0;
+    const size_t smem = PRO == PRO_RMS ? (size_t)(MT + 1) * p.K * sizeof(T) : 0;
     // persistent: as many CTAs as can be resident at once (registers decide:
     // 72-116 per thread give 2-3 CTAs of 256 threads per SM), each looping
     // over weight-row blocks, so no CTA waits for another to retire
@@ -324,7 +372,7 @@ int launch_ks(const DecodeGemvParams &p, cudaStream_t s) {
     // ... but not past the point where the blocks no longer fit in one wave
     // of resident CTAs when half the split would: a second wave costs a
     // whole extra HBM round trip for a few CTAs
-    const size_t smem = PRO == PRO_RMS ? (size_t)MT * p.K * sizeof(T) : 0;
+    const size_t smem = PRO == PRO_RMS ? (size_t)(MT + 1) * p.K * sizeof(T) : 0;
     const int ctas = sm_count() * resident_ctas<T, MT, 8, PRO, EPI>(smem);
     auto blocks = [&](int k) { return (p.groups + 8 / k - 1) / (8 / k); };
     while (ks > 1 && blocks(ks) > ctas && blocks(ks / 2) <= ctas && (nvec + ks / 2 - 1) / (ks / 2) <= 32 * kVPL)

@@ -39,29 +39,28 @@ __global__ void __launch_bounds__(kThreads) ew2_vec_kernel(T *__restrict__ out, 
                                                            const T *__restrict__ b, size_t nvec, size_t n, Op op) {
     constexpr int V = Vec16<T>::N;
     const size_t stride = (size_t)gridDim.x * kThreads;
-    size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x;
-    for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
+    // every pass requests all of its (up to kUnroll) vectors before the first
+    // use; the last pass is predicated rather than finished one vector per
+    // round trip
+    for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < nvec; i += kUnroll * stride) {
         Vec16<T> va[kUnroll], vb[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; u++) {
-            va[u].u = ld_global_nc_v4(a + (i + u * stride) * V);
-            vb[u].u = ld_global_nc_v4(b + (i + u * stride) * V);
+            if (i + u * stride < nvec) {
+                va[u].u = ld_global_nc_v4(a + (i + u * stride) * V);
+                vb[u].u = ld_global_nc_v4(b + (i + u * stride) * V);
+            }
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; u++) {
-            Vec16<T> vo;
+            if (i + u * stride < nvec) {
+                Vec16<T> vo;
 #pragma unroll
-            for (int e = 0; e < V; e++) vo.e[e] = Elem<T>::store(op(Elem<T>::load(va[u].e[e]), Elem<T>::load(vb[u].e[e])));
-            *reinterpret_cast<uint4 *>(out + (i + u * stride) * V) = vo.u;
+                for (int e = 0; e < V; e++)
+                    vo.e[e] = Elem<T>::store(op(Elem<T>::load(va[u].e[e]), Elem<T>::load(vb[u].e[e])));
+                *reinterpret_cast<uint4 *>(out + (i + u * stride) * V) = vo.u;
+            }
         }
-    }
-    for (; i < nvec; i += stride) {
-        Vec16<T> va, vb, vo;
-        va.u = ld_global_nc_v4(a + i * V);
-        vb.u = ld_global_nc_v4(b + i * V);
-#pragma unroll
-        for (int e = 0; e < V; e++) vo.e[e] = Elem<T>::store(op(Elem<T>::load(va.e[e]), Elem<T>::load(vb.e[e])));
-        *reinterpret_cast<uint4 *>(out + i * V) = vo.u;
     }
     // scalar tail
     if (blockIdx.x == 0) {
@@ -81,8 +80,14 @@ int launch_ew2(T *out, const T *a, const T *b, size_t n, cudaStream_t s, Op op, 
     constexpr int V = Vec16<T>::N;
     const int max_blocks = sm_count() * (2048 / kThreads);
     if (aligned16(out) && aligned16(a) && aligned16(b)) {
+        // passes per thread: as few as a full grid allows; then the fewest
+        // CTAs that cover the vectors in that many passes, so every thread
+        // has (nearly) the same number of vectors. One pass: spread the
+        // vectors over as many SMs as possible (one per thread).
         size_t nvec = n / V;
-        size_t want = (nvec + (size_t)kThreads * kUnroll - 1) / ((size_t)kThreads * kUnroll);
+        const size_t per_pass = (size_t)kThreads * kUnroll;
+        const size_t passes = (nvec + per_pass * max_blocks - 1) / (per_pass * max_blocks);
+        size_t want = passes > 1 ? (nvec + per_pass * passes - 1) / (per_pass * passes) : (nvec + kThreads - 1) / kThreads;
         int blocks = (int)(want < 1 ? 1 : (want > (size_t)max_blocks ? max_blocks : want));
         ew2_vec_kernel<T, Op><<<blocks, kThreads, 0, s>>>(out, a, b, nvec, n, op);
     } else {

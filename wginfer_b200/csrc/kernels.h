@@ -60,6 +60,14 @@ struct DecodeGemvParams {
     // [M0, K] scratch for the normalised rows when more than 8 rows take the
     // tensor-core path with the RMS prologue (may be null: GEMV chunks then)
     void *xn;
+    // split-K scratch of the tensor-core path (may be null: no split): an
+    // f32 accumulator tile per output tile and one arrival counter per
+    // output tile, both zero between launches (the last CTA of a tile
+    // clears them); launches that may overlap need separate scratch
+    float *tc_ws;
+    size_t tc_ws_bytes;
+    unsigned *tc_cnt;
+    int tc_cnt_n;
 };
 enum { DG_PRO_PLAIN = 0, DG_PRO_RMS = 1, DG_EPI_STORE = 0, DG_EPI_SWIGLU = 1, DG_EPI_ROPEKV = 2 };
 int decode_gemv(wginferDataType_t dtype, const DecodeGemvParams &p, int pro, int epi, cudaStream_t s);

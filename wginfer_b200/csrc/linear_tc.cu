@@ -1,20 +1,23 @@
 // Tensor-core GEMM for linear with more than 8 input rows (prefill, batched
 // decode): out[M, N] = X[M, K] . W[N, K]^T on the 5th-generation tensor cores.
 //
-// A CTA owns 128 weight rows (the MMA's M dimension, one TMEM lane each) and
-// TN input rows (the MMA's N dimension, TN in {16, 32, 64, 128, 256}); the
-// f32 accumulator tile [128 x TN] lives in tensor memory. Warp 0 streams
-// 64-wide K slices of W and X into a 4-stage shared-memory ring with TMA
-// (cp.async.bulk.tensor, 128-byte swizzle, no multicast); one thread of
-// warp 1 issues tcgen05.mma (kind::f16, bf16 in, f32 accumulate, 4 x K16 per
-// slice) and frees each stage with tcgen05.commit; after the last slice all
-// four warps read the accumulator with tcgen05.ld (warp w owns TMEM lanes
-// 32w..32w+31, i.e. weight rows) and run the same epilogues as the GEMV path
+// A work unit is 128 weight rows (the MMA's M dimension, one TMEM lane each)
+// x TN input rows (the MMA's N dimension, TN in {16, 32, 64, 128, 256}) x a
+// range of K; its f32 accumulator [128 x TN] lives in tensor memory. The
+// kernel is persistent (one CTA per SM, units strided over the grid) and
+// warp-specialised: warp 0 streams 64-wide K slices of W and X into a
+// shared-memory ring with TMA (cp.async.bulk.tensor, 128-byte swizzle, no
+// multicast); one thread of warp 1 issues tcgen05.mma (kind::f16, bf16 in,
+// f32 accumulate, 4 x K16 per slice), frees each stage with tcgen05.commit
+// and alternates between two TMEM accumulators; warps 2-5 read a finished
+// accumulator with tcgen05.ld (warp w owns TMEM lanes 32 (w % 4) ..., i.e.
+// weight rows) and run the same epilogues as the GEMV path
 // (decode_common.cuh): bias, residual, SwiGLU of adjacent gate/up rows, or
 // RoPE + K/V append of adjacent rotation partners (the partner's value comes
-// from the neighbouring lane by shuffle). Output writes are coalesced: for a
-// fixed input row, the 32 lanes of a warp write 32 consecutive outputs.
-// Roofline: tensor, 2*M*N*K flops.
+// from the neighbouring lane by shuffle), while the next unit's MMAs fill
+// the other accumulator. Output writes are coalesced: for a fixed input row,
+// the lanes of a warp write consecutive outputs. Roofline: tensor, 2*M*N*K
+// flops (HBM for a few input rows: the weights, N*K*2 bytes).
 //
 // Every mbarrier wait is bounded; on a stall the kernel records an error in
 // the device error word, skips the rest, waits (bounded) for copies in
@@ -30,7 +33,8 @@
 namespace wgb {
 namespace {
 
-constexpr int kTcThreads = 128;
+constexpr int kTcEpiWarps = 4;                     // epilogue warps (one per TMEM lane quarter)
+constexpr int kTcThreads = 32 * (2 + kTcEpiWarps);  // + the TMA producer and MMA issuer warps
 constexpr int kBK = 64;          // K elements per stage (128 bytes of bf16: one swizzle span)
 constexpr int kTcMaxStages = 8;
 constexpr int kTileW = 128;      // weight rows per CTA (MMA M)
@@ -105,10 +109,13 @@ __host__ __device__ inline uint32_t idesc_bf16(int tn) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(tn >> 3) << 17) | ((uint32_t)(kTileW >> 4) << 24);
 }
 
-// Stages in the ring: 4. Deeper rings for the narrow tiles were measured
-// slower: their shared memory halves the CTAs resident per SM, and a CTA's
-// throughput does not grow with its ring depth.
-inline int tc_stages(int) { return 4; }
+// Stages in the ring: as many as fit in about 192 KB (one CTA per SM), at
+// most kTcMaxStages: 8 for input tiles up to 64 rows, 6 for 128, 4 for 256.
+inline int tc_stages(int tn) {
+    const int st = kTileW * kBK * 2 + tn * kBK * 2;
+    const int n = (192 * 1024) / st;
+    return n > kTcMaxStages ? kTcMaxStages : n;
+}
 inline size_t tc_smem_bytes(int tn) {
     return 1024 + (size_t)tc_stages(tn) * ((size_t)kTileW * kBK * 2 + (size_t)tn * kBK * 2);
 }
@@ -118,35 +125,146 @@ inline size_t tc_smem_max() {
     return m;
 }
 
+// Epilogue of one chunk of up to 32 input rows: v[j] is this lane's f32 sum
+// for weight row n and input row m = mc + j (j < cols). All lanes take part
+// in the shuffle that hands each even lane its partner row's sum; even lanes
+// own the row pair (n, n + 1) and run the shared epilogue arithmetic
+// (decode_common.cuh). The per-row operands of the chunk (residuals,
+// positions, cos/sin) are loaded before its first store, so a chunk costs
+// one or two memory round trips rather than one per input row.
+template <int EPI>
+__device__ __forceinline__ void tc_epilogue(const DecodeGemvParams &p, int n, int mc, int cols, const float (&v)[32],
+                                            float b0, float b1) {
+    using T = __nv_bfloat16;
+    float pv[32];
+#pragma unroll
+    for (int j = 0; j < 32; j++) pv[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);
+    if ((threadIdx.x & 1) || n >= p.N) return;
+    const bool r1ok = n + 1 < p.N;
+    const int g = n >> 1;
+    if constexpr (EPI == EPI_STORE) {
+        T *out = reinterpret_cast<T *>(p.out);
+        const T *res = reinterpret_cast<const T *>(p.res);
+        float q0[32], q1[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int m = mc + j;
+            q0[j] = q1[j] = 0.f;
+            if (res && j < cols && m < p.M) {
+                q0[j] = ldf(res, (size_t)m * p.ldo + n);
+                if (r1ok) q1[j] = ldf(res, (size_t)m * p.ldo + n + 1);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int m = mc + j;
+            if (j < cols && m < p.M) {
+                float s0 = v[j] + b0, s1 = pv[j] + b1;
+                if (res) {
+                    s0 = __fadd_rn(q0[j], Elem<T>::load(Elem<T>::store(s0)));
+                    s1 = __fadd_rn(q1[j], Elem<T>::load(Elem<T>::store(s1)));
+                }
+                stf(out, (size_t)m * p.ldo + n, s0);
+                if (r1ok) stf(out, (size_t)m * p.ldo + n + 1, s1);
+            }
+        }
+    } else if constexpr (EPI == EPI_SWIGLU) {
+        T *out = reinterpret_cast<T *>(p.out);
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int m = mc + j;
+            if (j < cols && m < p.M) {
+                const float gg = Elem<T>::load(Elem<T>::store(v[j] + b0));
+                const float uu = Elem<T>::load(Elem<T>::store(pv[j] + b1));
+                stf(out, (size_t)m * p.ldo + g, __fdiv_rn(__fmul_rn(uu, gg), __fadd_rn(1.0f, expf(-gg))));
+            }
+        }
+    } else {
+        const int half = p.dh >> 1;
+        const int P = (p.nh + p.nkvh) * half;
+#pragma unroll
+        for (int h0 = 0; h0 < 32; h0 += 16) {
+            int64_t pos[16];
+            float2 cs[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int m = mc + h0 + j;
+                pos[j] = h0 + j < cols && m < p.M ? p.pos[m] : 0;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                cs[j] = make_float2(0.f, 0.f);
+                if (g < P && h0 + j < cols && pos[j] >= 0 && pos[j] < p.maxseq)
+                    cs[j] = p.table[(size_t)pos[j] * half + (g % half)];
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int m = mc + h0 + j;
+                if (h0 + j < cols && m < p.M)
+                    rope_kv_store<T>(p, g, r1ok, m, v[h0 + j] + b0, pv[h0 + j] + b1, pos[j], cs[j]);
+            }
+        }
+    }
+}
+
+// Work units of one launch: output tile t = (weight tile bx, input tile by)
+// and K split z; unit u = (t * ksplit + z), t = bx * tiles_m + by, so the
+// input tiles that share a weight tile (and the K splits of a tile) run on
+// neighbouring CTAs at the same time.
+struct TcSched {
+    int tiles_m, ksplit, kper, ktiles_total, nunits;
+    __device__ __forceinline__ void unit(int u, int tn, int &t, int &n0, int &m0, int &kb, int &nk) const {
+        const int z = u % ksplit;
+        t = u / ksplit;
+        n0 = (t / tiles_m) * kTileW;
+        m0 = (t % tiles_m) * tn;
+        kb = z * kper;
+        nk = min(kper, ktiles_total - kb);
+    }
+};
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiWarps * 32) : "memory"); }
+__device__ __forceinline__ void mb_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s_u32(b)) : "memory");
+}
+
+// Persistent and warp-specialised: warp 0 streams the K slices of this CTA's
+// units through the shared-memory ring (TMA), warp 1 issues the MMAs of
+// unit i into TMEM accumulator i % 2, warps 2-5 run the epilogue of unit i
+// from that accumulator while the MMAs of unit i + 1 fill the other one.
+// Warp w of the epilogue reads TMEM lanes 32 (w % 4) .. 32 (w % 4) + 31.
 template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, DecodeGemvParams p,
-                   int tn, int nst) {
+                   int tn, int nst, TcSched sc) {
     using T = __nv_bfloat16;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t full[kTcMaxStages], empty[kTcMaxStages], done;
+    __shared__ __align__(8) uint64_t full[kTcMaxStages], empty[kTcMaxStages], acc_full[2], acc_empty[2], done;
     __shared__ uint32_t s_tmem;
-    __shared__ int s_bad, s_issued;
+    __shared__ int s_bad, s_issued, s_last, s_stop[2], s_counted;
     unsigned char *smem = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int a_bytes = kTileW * kBK * 2, b_bytes = tn * kBK * 2, st_bytes = a_bytes + b_bytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kTileW, m0 = blockIdx.y * tn;
-    const int ktiles = (p.K + kBK - 1) / kBK;
-    const uint32_t ncols = tn <= 32 ? 32 : (uint32_t)tn;  // a power of two >= 32
+    const uint32_t ncols = tn <= 32 ? 32 : (uint32_t)tn;  // columns of one accumulator (a power of two >= 32)
 
     if (threadIdx.x == 0) {
         s_bad = 0;
         s_issued = 0;
+        s_counted = 0;
         for (int i = 0; i < nst; i++) {
             mb_init(&full[i], 1);
             mb_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mb_init(&acc_full[i], 1);
+            mb_init(&acc_empty[i], kTcEpiWarps);
         }
         mb_init(&done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_u32(&s_tmem)),
-                     "r"(ncols)
+                     "r"(2 * ncols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -157,69 +275,173 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     pdl_trigger();
     pdl_wait();  // X (and, for residuals, the output) come from the previous kernel
 
-    if (warp == 0 && lane == 0) {
-        // producer: TMA slices of W (128 rows) and X (tn rows) into the ring
-        for (int kt = 0; kt < ktiles; kt++) {
-            const int st = kt % nst;
-            if (kt >= nst && !mb_wait(&empty[st], (unsigned)(((kt / nst) - 1) & 1))) {
-                atomicExch(&s_bad, 1);
-                break;
+    if (warp == 0) {
+        if (lane == 0) {
+            // producer: TMA slices of W (128 rows) and X (tn rows) into the ring
+            int it = 0;
+            for (int u = blockIdx.x; u < sc.nunits; u += gridDim.x) {
+                int t, n0, m0, kb, nk;
+                sc.unit(u, tn, t, n0, m0, kb, nk);
+                for (int kt = 0; kt < nk; kt++, it++) {
+                    const int st = it % nst;
+                    if (it >= nst && !mb_wait(&empty[st], (unsigned)(((it / nst) - 1) & 1))) {
+                        atomicExch(&s_bad, 1);
+                        break;
+                    }
+                    unsigned char *a = smem + (size_t)st * st_bytes;
+                    mb_expect_tx(&full[st], (unsigned)st_bytes);
+                    tma_load_2d(a, &tmW, (kb + kt) * kBK, n0, &full[st]);
+                    tma_load_2d(a + a_bytes, &tmX, (kb + kt) * kBK, m0, &full[st]);
+                    s_issued = it + 1;
+                }
+                if (*(volatile int *)&s_bad) break;
             }
-            unsigned char *a = smem + (size_t)st * st_bytes;
-            mb_expect_tx(&full[st], (unsigned)st_bytes);
-            tma_load_2d(a, &tmW, kt * kBK, n0, &full[st]);
-            tma_load_2d(a + a_bytes, &tmX, kt * kBK, m0, &full[st]);
-            s_issued = kt + 1;
         }
-    } else if (warp == 1 && lane == 0) {
-        // MMA issuer
-        const uint32_t idesc = idesc_bf16(tn);
-        for (int kt = 0; kt < ktiles; kt++) {
-            const int st = kt % nst;
-            if (!mb_wait(&full[st], (unsigned)((kt / nst) & 1))) {
-                atomicExch(&s_bad, 1);
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // MMA issuer
+            const uint32_t idesc = idesc_bf16(tn);
+            int it = 0, i = 0;
+            for (int u = blockIdx.x; u < sc.nunits; u += gridDim.x, i++) {
+                int t, n0, m0, kb, nk;
+                sc.unit(u, tn, t, n0, m0, kb, nk);
+                const int buf = i & 1, use = i >> 1;
+                if (use >= 1 && !mb_wait(&acc_empty[buf], (unsigned)((use - 1) & 1))) {
+                    atomicExch(&s_bad, 1);
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t d = tmem + (uint32_t)buf * ncols;
+                bool ok = true;
+                for (int kt = 0; kt < nk; kt++, it++) {
+                    const int st = it % nst;
+                    if (!mb_wait(&full[st], (unsigned)((it / nst) & 1))) {
+                        atomicExch(&s_bad, 1);
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const unsigned char *a = smem + (size_t)st * st_bytes;
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; k++)
+                        mma_bf16(d, sw128_desc(a + k * 32), sw128_desc(a + a_bytes + k * 32), idesc, (kt | k) != 0);
+                    mma_commit(&empty[st]);  // the stage is free once these MMAs have read it
+                }
+                if (!ok) break;
+                mma_commit(&acc_full[buf]);  // the accumulator is complete once they have run
+            }
+            mma_commit(&done);
+        }
+    } else {
+        // epilogue warps
+        const int q = warp & 3;  // TMEM lane quarter
+        const int row = q * 32 + lane;
+        const bool leader = warp == 2 && lane == 0;
+        int i = 0;
+        for (int u = blockIdx.x; u < sc.nunits; u += gridDim.x, i++) {
+            int t, n0, m0, kb, nk;
+            sc.unit(u, tn, t, n0, m0, kb, nk);
+            const int buf = i & 1, use = i >> 1;
+            // one thread waits for the accumulator; the decision to go on is
+            // shared through s_stop so the four warps never part at a barrier
+            if (leader) s_stop[i & 1] = !mb_wait(&acc_full[buf], (unsigned)(use & 1)) || *(volatile int *)&s_bad;
+            epi_bar();
+            if (s_stop[i & 1]) {
+                if (leader) atomicExch(&s_bad, 1);
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const unsigned char *a = smem + (size_t)st * st_bytes;
+            const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)buf * ncols;
+            const int n = n0 + row;
+            float b0 = 0.f, b1 = 0.f;  // the row pair's bias, loaded once per unit
+            if (p.bias && (lane & 1) == 0 && n < p.N) {
+                b0 = ldf(reinterpret_cast<const T *>(p.bias), n);
+                if (n + 1 < p.N) b1 = ldf(reinterpret_cast<const T *>(p.bias), n + 1);
+            }
+            if (sc.ksplit > 1) {
+                // split-K: add this unit's partial tile into the tile's f32
+                // accumulator ([tn][128], lanes contiguous; reductions in L2);
+                // the CTA that arrives last reads the sums, runs the epilogue
+                // and clears the accumulator and the counter for the next launch
+                float *ws = p.tc_ws + (size_t)t * 128 * tn;
+                for (int c0 = 0; c0 < tn; c0 += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(acc + (uint32_t)c0, r);
 #pragma unroll
-            for (int k = 0; k < kBK / 16; k++)
-                mma_bf16(tmem, sw128_desc(a + k * 32), sw128_desc(a + a_bytes + k * 32), idesc, (kt | k) != 0);
-            mma_commit(&empty[st]);  // the stage is free once these MMAs have read it
-        }
-        mma_commit(&done);
-    }
-    __syncwarp();
-    // epilogue: all four warps; warp w reads TMEM lanes 32w..32w+31 (weight rows)
-    if (!mb_wait(&done, 0)) atomicExch(&s_bad, 1);
-    __syncthreads();
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const bool ok = !s_bad;
-    if (ok) {
-        const int n = n0 + warp * 32 + lane;
-        for (int c0 = 0; c0 < tn; c0 += 32) {
-            uint32_t r[32];
-            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+                    for (int j = 0; j < 32; j++)
+                        if (c0 + j < tn) atomicAdd(ws + (size_t)(c0 + j) * 128 + row, __uint_as_float(r[j]));
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mb_arrive(&acc_empty[buf]);
+                __threadfence();
+                epi_bar();
+                if (leader) {
+                    s_last = atomicAdd(&p.tc_cnt[t], 1u) == (unsigned)(sc.ksplit - 1);
+                    s_counted = 1;
+                }
+                epi_bar();
+                if (s_last) {
+                    __threadfence();
+                    for (int c0 = 0; c0 < tn; c0 += 32) {
+                        float v[32];
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const float v = __uint_as_float(r[j]);
-                const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
-                const int m = m0 + c0 + j;
-                if ((lane & 1) == 0 && c0 + j < tn && m < p.M && n < p.N)
-                    epilogue<T, EPI>(p, n >> 1, n, n + 1, n + 1 < p.N, m, v, partner);
+                        for (int j = 0; j < 32; j++)
+                            v[j] = c0 + j < tn ? __ldcg(ws + (size_t)(c0 + j) * 128 + row) : 0.f;
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (c0 + j < tn) __stcg(ws + (size_t)(c0 + j) * 128 + row, 0.f);
+                        tc_epilogue<EPI>(p, n, m0 + c0, min(32, tn - c0), v, b0, b1);
+                    }
+                    if (leader) p.tc_cnt[t] = 0;
+                }
+                epi_bar();  // s_last is rewritten by the next unit
+            } else {
+                for (int c0 = 0; c0 < tn; c0 += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(acc + (uint32_t)c0, r);
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+                    if (c0 + 32 >= tn) {  // last chunk read: the MMAs may refill this accumulator
+                        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) mb_arrive(&acc_empty[buf]);
+                    }
+                    tc_epilogue<EPI>(p, n, m0 + c0, min(32, tn - c0), v, b0, b1);
+                }
             }
         }
-    } else if (threadIdx.x == 0) {
-        record_device_error(p.err, 6, blockIdx.x);
-        // TMA copies may still be landing in the ring: wait (bounded) for
-        // the last one issued into each stage before the CTA exits
-        for (int kt = s_issued - 1; kt >= 0 && kt >= s_issued - nst; kt--)
-            mb_wait(&full[kt % nst], (unsigned)((kt / nst) & 1));
     }
+    __syncwarp();
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
+    if (threadIdx.x == 0) {
+        // every MMA this CTA issued has completed (tracked by `done`)
+        if (!mb_wait(&done, 0)) s_bad = 1;
+        if (s_bad) {
+            record_device_error(p.err, 6, blockIdx.x);
+            // TMA copies may still be landing in the ring: wait (bounded) for
+            // the last one issued into each stage before the CTA exits
+            for (int it = s_issued - 1; it >= 0 && it >= s_issued - nst; it--)
+                mb_wait(&full[it % nst], (unsigned)((it / nst) & 1));
+            // split-K (one unit per CTA): arrive for the unit if the epilogue
+            // did not, so the tile's counter and accumulator end up cleared
+            if (sc.ksplit > 1 && !s_counted && (int)blockIdx.x < sc.nunits) {
+                int t, n0, m0, kb, nk;
+                sc.unit(blockIdx.x, tn, t, n0, m0, kb, nk);
+                if (atomicAdd(&p.tc_cnt[t], 1u) == (unsigned)(sc.ksplit - 1)) {
+                    float *ws = p.tc_ws + (size_t)t * 128 * tn;
+                    for (int e = 0; e < 128 * tn; e++) __stcg(ws + e, 0.f);
+                    p.tc_cnt[t] = 0;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (warp == 1)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * ncols) : "memory");
 }
 
 // ---- host: tensor maps through the driver entry point (not linked) ----
@@ -264,9 +486,50 @@ int pick_tn(int M, int N) {
     return tn;
 }
 
+// Split-K plan for up to 64 input rows: when the weight tiles cannot fill
+// half the SMs, keep the widest input tile (the weights are read once) and
+// split K across CTAs instead, as many splits as fit in one wave; the
+// partial sums meet in an f32 accumulator in L2 (tc_ws, one [tn][128] tile
+// per output tile, zero between launches). The order in which the splits
+// add up varies from run to run (FAST numerics: f32 sums in any order).
+// Otherwise ksplit = 1 and the input tile comes from pick_tn.
+void plan_split(const DecodeGemvParams &p, int &tn, int &ksplit, int &kper) {
+    const int ktiles = (p.K + kBK - 1) / kBK;
+    ksplit = 1;
+    kper = ktiles;
+    int wide = 16;
+    while (wide < p.M && wide < 256) wide *= 2;
+    const long long tiles = (long long)((p.N + kTileW - 1) / kTileW) * ((p.M + wide - 1) / wide);
+    const long long sms = sm_count();
+    if (p.tc_ws && p.tc_cnt && wide <= 64 && 2 * tiles <= sms && tiles <= p.tc_cnt_n && ktiles >= 2 &&
+        (size_t)tiles * 128 * wide * sizeof(float) <= p.tc_ws_bytes) {
+        int ks = (int)(sms / tiles);
+        if (ks > ktiles) ks = ktiles;
+        if (ks > 32) ks = 32;
+        const int per = (ktiles + ks - 1) / ks;
+        ks = (ktiles + per - 1) / per;  // every split gets at least one slice
+        if (ks > 1) {
+            tn = wide;
+            ksplit = ks;
+            kper = per;
+            return;
+        }
+    }
+    tn = pick_tn(p.M, p.N);
+}
+
 template <int EPI>
 int launch_tc(const DecodeGemvParams &p, cudaStream_t s) {
-    const int tn = pick_tn(p.M, p.N);
+    int tn, ksplit, kper;
+    plan_split(p, tn, ksplit, kper);
+    TcSched sc;
+    sc.tiles_m = (p.M + tn - 1) / tn;
+    sc.ksplit = ksplit;
+    sc.kper = kper;
+    sc.ktiles_total = (p.K + kBK - 1) / kBK;
+    const long long units = (long long)((p.N + kTileW - 1) / kTileW) * sc.tiles_m * ksplit;
+    if (units > (1ll << 30)) return set_error(WGB_ERR_INVALID_ARGUMENT, "linear(tc): too many tiles");
+    sc.nunits = (int)units;
     CUtensorMap tmW, tmX;
     if (!make_map(&tmW, p.w, p.N, p.K, kTileW) || !make_map(&tmX, p.x, p.M, p.K, tn))
         return set_error(WGB_ERR_CUDA, "linear(tc): tensor map encoding failed");
@@ -281,7 +544,9 @@ int launch_tc(const DecodeGemvParams &p, cudaStream_t s) {
         if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((p.N + kTileW - 1) / kTileW), (unsigned)((p.M + tn - 1) / tn));
+    // persistent: one CTA per SM (its ring takes most of the shared memory),
+    // each taking units blockIdx.x, blockIdx.x + gridDim.x, ...
+    cfg.gridDim = dim3((unsigned)(sc.nunits < sm_count() ? sc.nunits : sm_count()));
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = tc_smem_bytes(tn);
     cfg.stream = s;
@@ -290,7 +555,7 @@ int launch_tc(const DecodeGemvParams &p, cudaStream_t s) {
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI>, tmW, tmX, p, tn, tc_stages(tn));
+    cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI>, tmW, tmX, p, tn, tc_stages(tn), sc);
     if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "linear(tc): %s", cudaGetErrorString(e));
     return WGB_OK;
 }
@@ -298,7 +563,7 @@ int launch_tc(const DecodeGemvParams &p, cudaStream_t s) {
 }  // namespace
 
 bool tc_gemm_ok(const DecodeGemvParams &p) {
-    // TMA: 16-byte aligned bases and row strides; grid.y = M / tn <= 65535
+    // TMA: 16-byte aligned bases and row strides
     return p.M > 8 && p.K > 0 && p.K % 8 == 0 && aligned16(p.w) && aligned16(p.x) && p.N >= 1 && encode_fn() &&
            p.M <= 128 * 65535 && p.N < (1 << 30);
 }

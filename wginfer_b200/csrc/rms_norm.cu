@@ -37,7 +37,7 @@ __global__ void __launch_bounds__(256) rms_warp_kernel(T *__restrict__ out, cons
         int vi = lane + u * 32;
         if (vi < nvec) {
             r[u].u = ld_global_nc_v4(x + (size_t)vi * V);
-            wr[u].u = ld_global_nc_v4(w + (size_t)vi * V);
+            wr[u].u = ld_global_l1_v4(w + (size_t)vi * V);  // every row reads w: keep it in L1
         }
     }
 #pragma unroll
@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(256) rms_block_kernel(T *__restrict__ out, con
         int vi = threadIdx.x + u * 256;
         if (vi < nvec) {
             r[u].u = ld_global_nc_v4(x + (size_t)vi * V);
-            wr[u].u = ld_global_nc_v4(w + (size_t)vi * V);
+            wr[u].u = ld_global_l1_v4(w + (size_t)vi * V);  // every row reads w: keep it in L1
         }
     }
 #pragma unroll
