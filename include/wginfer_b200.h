@@ -86,6 +86,19 @@ __export int wgb_argmax_rows(int64_t *max_idx, void *max_val, const void *vals,
                              wginferDataType_t dtype, size_t rows, size_t numel,
                              wginferStream_t stream);
 
+/* Row-wise sampling over logits[rows, vocab] (contiguous) into out_idx[rows]
+ * with the rules of the reference's host sampler sample_from_logits
+ * (src/models/qwen2/model.cpp:60-137), which copies the logits to the host
+ * and sorts them; here the whole draw stays on the device. temperature <= 0,
+ * or top_k == 1 with top_p >= 1, gives the argmax; top_k outside [1, vocab]
+ * means vocab; top_p outside (0, 1] means 1. Logits that compare equal are
+ * ordered by index; NaN logits are never drawn unless all are NaN. The
+ * random number of row r is a hash of (seed, offset, r): the same arguments
+ * give the same tokens. New entry for batched decode. */
+__export int wgb_sample_rows(int64_t *out_idx, const void *logits, wginferDataType_t dtype, size_t rows,
+                             size_t vocab, int top_k, float top_p, float temperature, unsigned long long seed,
+                             unsigned long long offset, wginferStream_t stream);
+
 /* out[i, :] = weight[index[i], :]. Replaces ops::nvidia::embedding
  * (src/ops/embedding/nvidia/embedding_nvidia.cuh:6-8); `vocab` (weight rows,
  * known to the op front as weight->shape()[0]) is added so that an index

@@ -223,3 +223,43 @@ class ReferenceQwen2:
         if getattr(self, "h", None):
             self.ref.lib.ref_qwen2_destroy(C.c_void_p(self.h))
             self.h = None
+
+
+def sample_kept(logits: np.ndarray, top_k: int, top_p: float, temperature: float):
+    """The kept set of the reference's host sampler, sample_from_logits
+    (src/models/qwen2/model.cpp:60-137), for f32 logits: (indices in
+    decreasing logit order, their weights). Logits that compare equal are
+    taken in index order (the reference's partial_sort leaves them in an
+    unspecified order). temperature <= 0 or top_k == 1 with top_p >= 1 give
+    the argmax alone (weight 1)."""
+    lg = np.asarray(logits, dtype=np.float32).reshape(-1)
+    vocab = lg.size
+    if not temperature > 0.0:
+        return np.array([int(np.argmax(lg))]), np.array([1.0])
+    if top_k <= 0 or top_k > vocab:
+        top_k = vocab
+    if not top_p > 0.0 or top_p > 1.0:
+        top_p = 1.0
+    if top_k == 1 and top_p >= 1.0:
+        return np.array([int(np.argmax(lg))]), np.array([1.0])
+    order = np.argsort(-lg, kind="stable")[:top_k]          # model.cpp:84-93
+    inv_temp = np.float32(1.0) / np.float32(temperature)    # :96
+    scaled = (lg[order] * inv_temp).astype(np.float32)
+    max_scaled = scaled.max()                               # :97-100
+    probs = np.exp((scaled - max_scaled).astype(np.float32).astype(np.float64))  # :103-111
+    probs[~np.isfinite(probs) | (probs < 0)] = 0.0
+    total = 0.0
+    for p in probs:
+        total += p
+    if top_p < 1.0:                                         # :117-130
+        cum, keep = 0.0, 0
+        tp = float(np.float32(top_p))
+        for i, p in enumerate(probs):
+            cum += p / total
+            keep = i + 1
+            if cum >= tp:
+                break
+        keep = max(keep, 1)
+        order, probs = order[:keep], probs[:keep]
+    return order, probs
+

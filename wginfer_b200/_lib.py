@@ -31,6 +31,7 @@ SIGNATURES = {
     "wgb_add": (_I, [_P, _P, _P, _I, _S, _P]),
     "wgb_argmax": (_I, [_P, _P, _P, _I, _S, _P]),
     "wgb_argmax_rows": (_I, [_P, _P, _P, _I, _S, _S, _P]),
+    "wgb_sample_rows": (_I, [_P, _P, _I, _S, _S, _I, _F, _F, C.c_ulonglong, C.c_ulonglong, _P]),
     "wgb_embedding": (_I, [_P, _P, _P, _I, _S, _S, _S, _P]),
     "wgb_linear": (_I, [_P, _P, _P, _P, _I, _S, _S, _S, _P]),
     "wgb_rms_norm": (_I, [_P, _P, _P, _I, _S, _S, _F, _P]),

@@ -92,6 +92,20 @@ def argmax_rows(max_idx, max_val, vals):
                                               vals.shape[1], _stream(vals)), "argmax_rows")
 
 
+def sample_rows(out_idx, logits, top_k=0, top_p=1.0, temperature=1.0, seed=0, offset=0):
+    """Top-k / top-p / temperature sampling of each row of logits[B, V] on the
+    device, with the reference's rules (src/models/qwen2/model.cpp:60-137)."""
+    _same_device(out_idx, logits)
+    _arg(logits.dim() == 2, "logits must be 2D [rows, vocab]")
+    _arg(out_idx.numel() == logits.shape[0] and out_idx.dtype == torch.int64, "out_idx must be int64 [rows]")
+    _contig("tensors must be contiguous", out_idx, logits)
+    with torch.cuda.device(logits.device):
+        _lib.check(_lib.lib().wgb_sample_rows(_ptr(out_idx), _ptr(logits), _dt(logits), logits.shape[0],
+                                              logits.shape[1], int(top_k), float(top_p), float(temperature),
+                                              int(seed) & (2**64 - 1), int(offset) & (2**64 - 1),
+                                              _stream(logits)), "sample_rows")
+
+
 def embedding(out, index, weight):
     """src/ops/embedding/op.cpp:15-66."""
     _same_device(out, index, weight)
