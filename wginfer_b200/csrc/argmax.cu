@@ -5,7 +5,11 @@
 // many rows, so that all CTAs fit in one wave): each CTA reduces
 // its slice with 16-byte loads to one 64-bit key per CTA, and CTA 0 of the
 // cluster folds the keys of the others through distributed shared memory,
-// so no global scratch and no second launch are needed. Key = (order-
+// so no global scratch and no second launch are needed. Per 16-byte vector a
+// thread does a branch-free max tree and one compare with its running
+// maximum, remembering the first vector that set it; the element index is
+// found once, at the end, by re-reading that vector. (An element-wise
+// compare-and-select chain made the op instruction-bound at bf16.) Key = (order-
 // preserving bits of the value) << 32 | (0xFFFFFFFF - index): the largest
 // key is the largest value at the smallest index. -0 is folded into +0
 // (they compare equal under '>'); NaN never wins unless it is element 0,
@@ -23,7 +27,8 @@ namespace wgb {
 namespace {
 
 constexpr int kCluster = 8;
-constexpr int kThreads = 512;
+constexpr int kThreads = 256;
+constexpr int kB = 4;  // 16-byte vectors in flight per thread
 
 __device__ __forceinline__ unsigned long long make_key(float v, uint32_t idx) {
     if (v == 0.f) v = 0.f;  // -0 -> +0
@@ -47,34 +52,25 @@ __device__ __forceinline__ void consider(Best &b, T x, uint32_t idx) {
         b.i = idx;
     }
 }
-// Maximum of a 16-byte vector (NaN ignored unless every element is NaN).
+// Maximum of a 16-byte vector by a max tree (NaN operands lose to numbers;
+// a vector of NaN only gives NaN).
 template <typename T> __device__ __forceinline__ float vec_max(const Vec16<T> &r);
 template <> __device__ __forceinline__ float vec_max<__nv_bfloat16>(const Vec16<__nv_bfloat16> &r) {
     const __nv_bfloat162 *p = reinterpret_cast<const __nv_bfloat162 *>(&r.u);
     const __nv_bfloat162 m = __hmax2(__hmax2(p[0], p[1]), __hmax2(p[2], p[3]));
-    return fmaxf(__low2float(m), __high2float(m));
+    return Elem<__nv_bfloat16>::load(__hmax(__low2bfloat16(m), __high2bfloat16(m)));
 }
 template <> __device__ __forceinline__ float vec_max<__half>(const Vec16<__half> &r) {
     const __half2 *p = reinterpret_cast<const __half2 *>(&r.u);
     const __half2 m = __hmax2(__hmax2(p[0], p[1]), __hmax2(p[2], p[3]));
-    return fmaxf(__low2float(m), __high2float(m));
+    return __half2float(__hmax(__low2half(m), __high2half(m)));
 }
-// A whole vector: 16-bit types compare the vector's maximum first and scan
-// the elements (in index order, as above) only when it beats the running
-// best, which is exactly when a scan could change it.
-template <typename T>
-__device__ __forceinline__ void consider_vec(Best &b, const Vec16<T> &r, uint32_t idx0) {
-    constexpr int V = Vec16<T>::N;
-    if constexpr (sizeof(T) == 2) {
-        const float vm = vec_max<T>(r);
-        if (!(vm > b.v || (b.i == 0xFFFFFFFFu && !isnan(vm)))) return;
-    }
-#pragma unroll
-    for (int e = 0; e < V; e++) consider(b, r.e[e], idx0 + e);
+template <> __device__ __forceinline__ float vec_max<float>(const Vec16<float> &r) {
+    return fmaxf(fmaxf(r.e[0], r.e[1]), fmaxf(r.e[2], r.e[3]));
 }
 
 template <typename T, bool kVec>
-__global__ void __launch_bounds__(kThreads) argmax_cluster_kernel(int64_t *max_idx, T *max_val, const T *vals,
+__global__ void __launch_bounds__(kThreads, 4) argmax_cluster_kernel(int64_t *max_idx, T *max_val, const T *vals,
                                                                   size_t numel) {
     constexpr int V = Vec16<T>::N;
     __shared__ unsigned long long red[kThreads / 32];
@@ -88,17 +84,35 @@ __global__ void __launch_bounds__(kThreads) argmax_cluster_kernel(int64_t *max_i
         const size_t nvec = numel / V;
         const size_t per = (nvec + ns - 1) / ns;
         const size_t v0 = rank * per < nvec ? rank * per : nvec, v1 = v0 + per < nvec ? v0 + per : nvec;
-        // batches of 8 vectors per thread, the last batch predicated, so a
-        // thread's slice costs ceil(slice / 8) round trips
-        constexpr int kB = 8;
+        // batches of kB vectors per thread, the last batch predicated, so a
+        // thread's slice costs ceil(slice / kB) round trips; per vector one
+        // compare: the first vector (in index order) holding the thread's
+        // maximum is remembered
+        float best = -INFINITY;
+        long long bvec = -1;
         for (size_t i = v0 + threadIdx.x; i < v1; i += kB * kThreads) {
             Vec16<T> r[kB];
 #pragma unroll
             for (int u = 0; u < kB; u++)
                 if (i + u * kThreads < v1) r[u].u = ld_global_nc_v4(x + (i + u * kThreads) * V);
 #pragma unroll
-            for (int u = 0; u < kB; u++)
-                if (i + u * kThreads < v1) consider_vec(bt, r[u], (uint32_t)((i + u * kThreads) * V));
+            for (int u = 0; u < kB; u++) {
+                if (i + u * kThreads < v1) {
+                    const float m = vec_max<T>(r[u]);
+                    if (m > best || (bvec < 0 && m == m)) {
+                        best = m;
+                        bvec = (long long)(i + u * kThreads);
+                    }
+                }
+            }
+        }
+        if (bvec >= 0) {  // the first element of that vector equal to the maximum
+            Vec16<T> r;
+            r.u = ld_global_nc_v4(x + (size_t)bvec * V);
+#pragma unroll
+            for (int e = V - 1; e >= 0; e--)
+                if (Elem<T>::load(r.e[e]) == best) bt.i = (uint32_t)(bvec * V + e);
+            bt.v = best;
         }
     } else {
         const size_t per = (numel + ns - 1) / ns;
