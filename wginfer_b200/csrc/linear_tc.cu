@@ -15,8 +15,9 @@
 // (decode_common.cuh): bias, residual, SwiGLU of adjacent gate/up rows, or
 // RoPE + K/V append of adjacent rotation partners (the partner's value comes
 // from the neighbouring lane by shuffle), while the next unit's MMAs fill
-// the other accumulator. Output writes are coalesced: for a fixed input row,
-// the lanes of a warp write consecutive outputs. Roofline: tensor, 2*M*N*K
+// the other accumulator. The epilogue stages each 32-input-row chunk as
+// bf16 in shared memory and then writes it (and reads residuals) in 16-byte
+// pieces of 8 adjacent outputs. Roofline: tensor, 2*M*N*K
 // flops (HBM for a few input rows: the weights, N*K*2 bytes).
 //
 // Every mbarrier wait is bounded; on a stall the kernel records an error in
@@ -38,6 +39,8 @@ constexpr int kTcThreads = 32 * (2 + kTcEpiWarps);  // + the TMA producer and MM
 constexpr int kBK = 64;          // K elements per stage (128 bytes of bf16: one swizzle span)
 constexpr int kTcMaxStages = 8;
 constexpr int kTileW = 128;      // weight rows per CTA (MMA M)
+constexpr int kEpiRows = 32;  // input rows per epilogue chunk
+constexpr size_t kEpiTileBytes = (size_t)kEpiRows * kTileW * 2;  // its bf16 staging tile
 constexpr long long kTcWaitCycles = 4000000000ll;  // a stage stalled this long (about 2 s) counts as a failure
 
 __device__ __forceinline__ uint32_t s_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -117,7 +120,7 @@ inline int tc_stages(int tn) {
     return n > kTcMaxStages ? kTcMaxStages : n;
 }
 inline size_t tc_smem_bytes(int tn) {
-    return 1024 + (size_t)tc_stages(tn) * ((size_t)kTileW * kBK * 2 + (size_t)tn * kBK * 2);
+    return 1024 + (size_t)tc_stages(tn) * ((size_t)kTileW * kBK * 2 + (size_t)tn * kBK * 2) + kEpiTileBytes;
 }
 inline size_t tc_smem_max() {
     size_t m = 0;
@@ -125,83 +128,151 @@ inline size_t tc_smem_max() {
     return m;
 }
 
-// Epilogue of one chunk of up to 32 input rows: v[j] is this lane's f32 sum
-// for weight row n and input row m = mc + j (j < cols). All lanes take part
-// in the shuffle that hands each even lane its partner row's sum; even lanes
-// own the row pair (n, n + 1) and run the shared epilogue arithmetic
-// (decode_common.cuh). The per-row operands of the chunk (residuals,
-// positions, cos/sin) are loaded before its first store, so a chunk costs
-// one or two memory round trips rather than one per input row.
-template <int EPI>
-__device__ __forceinline__ void tc_epilogue(const DecodeGemvParams &p, int n, int mc, int cols, const float (&v)[32],
-                                            float b0, float b1) {
-    using T = __nv_bfloat16;
-    float pv[32];
+// Loads the epilogue issues for a whole chunk before its first store. As
+// volatile asm with a memory clobber they stay in program order ahead of the
+// stores; as plain loads the compiler sank each one next to its use, behind
+// the previous row's stores (which may alias), so the chunk cost one memory
+// round trip per row instead of one in all.
+__device__ __forceinline__ float ld_bf16_early(const __nv_bfloat16 *p) {
+    unsigned short h;
+    asm volatile("ld.global.u16 %0, [%1];" : "=h"(h) : "l"(p) : "memory");
+    return __uint_as_float((uint32_t)h << 16);
+}
+__device__ __forceinline__ uint4 ld_global_v4_early(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p) : "memory");
+    return r;
+}
+__device__ __forceinline__ float ld_f32_early(const float *p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ int64_t ld_s64_early(const int64_t *p) {
+    long long v;
+    asm volatile("ld.global.s64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return (int64_t)v;
+}
+__device__ __forceinline__ float2 ld_f2_early(const float2 *p) {
+    float2 v;
+    asm volatile("ld.global.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p) : "memory");
+    return v;
+}
+
+// The epilogue of a chunk of up to 32 input rows runs in two phases through
+// a shared-memory tile S[32][128] of bf16 (input row j, weight row r):
+//   stage: each epilogue thread owns one weight row (its TMEM lane) and
+//          writes round(sum + bias) for the chunk's input rows (one column
+//          of S per thread: conflict-free);
+//   emit:  the 128 threads then take 16-byte pieces of S rows (8 adjacent
+//          weight rows of one input row), so residual loads and output
+//          stores are coalesced 16-byte accesses, all loads of a thread
+//          requested before its first store.
+// (A thread that walked its 32 input rows itself issued scattered 2-byte
+// accesses one row at a time; that cost one memory round trip per row.)
+
+__device__ __forceinline__ void tc_epi_stage(__nv_bfloat16 *S, int row, const float (&v)[32], float b) {
 #pragma unroll
-    for (int j = 0; j < 32; j++) pv[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);
-    if ((threadIdx.x & 1) || n >= p.N) return;
-    const bool r1ok = n + 1 < p.N;
-    const int g = n >> 1;
+    for (int j = 0; j < kEpiRows; j++) S[j * kTileW + row] = __float2bfloat16_rn(v[j] + b);
+}
+
+template <int EPI>
+__device__ __forceinline__ void tc_epi_emit(const DecodeGemvParams &p, const __nv_bfloat16 *S, int n0, int mc,
+                                            int cols, int et) {
+    using T = __nv_bfloat16;
+    constexpr int kPer = kEpiRows * kTileW / 8 / (kTcEpiWarps * 32);  // 16-byte pieces per thread (4)
+    const int nc = (et & 15) * 8;                                        // first weight row of the piece
+    const int jb = et >> 4;                                              // input rows jb, jb + 8, ...
+    Vec16<T> sv[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; k++) sv[k].u = *reinterpret_cast<const uint4 *>(S + (jb + 8 * k) * kTileW + nc);
     if constexpr (EPI == EPI_STORE) {
         T *out = reinterpret_cast<T *>(p.out);
         const T *res = reinterpret_cast<const T *>(p.res);
-        float q0[32], q1[32];
+        const bool vec = n0 + nc + 8 <= p.N && (p.ldo & 7) == 0 && ((uintptr_t)out & 15) == 0 &&
+                         ((uintptr_t)res & 15) == 0;
+        Vec16<T> rv[kPer];
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-            const int m = mc + j;
-            q0[j] = q1[j] = 0.f;
+        for (int k = 0; k < kPer; k++) {
+            const int j = jb + 8 * k, m = mc + j;
+            rv[k].u = make_uint4(0, 0, 0, 0);
             if (res && j < cols && m < p.M) {
-                q0[j] = ldf(res, (size_t)m * p.ldo + n);
-                if (r1ok) q1[j] = ldf(res, (size_t)m * p.ldo + n + 1);
+                const size_t o = (size_t)m * p.ldo + n0 + nc;
+                if (vec) {
+                    rv[k].u = ld_global_v4_early(res + o);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; e++)
+                        if (n0 + nc + e < p.N) rv[k].e[e] = __float2bfloat16_rn(ld_bf16_early(res + o + e));
+                }
             }
         }
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-            const int m = mc + j;
-            if (j < cols && m < p.M) {
-                float s0 = v[j] + b0, s1 = pv[j] + b1;
-                if (res) {
-                    s0 = __fadd_rn(q0[j], Elem<T>::load(Elem<T>::store(s0)));
-                    s1 = __fadd_rn(q1[j], Elem<T>::load(Elem<T>::store(s1)));
-                }
-                stf(out, (size_t)m * p.ldo + n, s0);
-                if (r1ok) stf(out, (size_t)m * p.ldo + n + 1, s1);
+        for (int k = 0; k < kPer; k++) {
+            const int j = jb + 8 * k, m = mc + j;
+            if (j >= cols || m >= p.M) continue;
+            Vec16<T> o;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const float x = Elem<T>::load(sv[k].e[e]);
+                o.e[e] = res ? __float2bfloat16_rn(__fadd_rn(Elem<T>::load(rv[k].e[e]), x)) : sv[k].e[e];
+            }
+            const size_t off = (size_t)m * p.ldo + n0 + nc;
+            if (vec) {
+                *reinterpret_cast<uint4 *>(out + off) = o.u;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; e++)
+                    if (n0 + nc + e < p.N) out[off + e] = o.e[e];
             }
         }
     } else if constexpr (EPI == EPI_SWIGLU) {
+        // rows (2g, 2g + 1) are gate and up of output g
         T *out = reinterpret_cast<T *>(p.out);
+        const int g0 = (n0 + nc) >> 1;
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-            const int m = mc + j;
-            if (j < cols && m < p.M) {
-                const float gg = Elem<T>::load(Elem<T>::store(v[j] + b0));
-                const float uu = Elem<T>::load(Elem<T>::store(pv[j] + b1));
-                stf(out, (size_t)m * p.ldo + g, __fdiv_rn(__fmul_rn(uu, gg), __fadd_rn(1.0f, expf(-gg))));
+        for (int k = 0; k < kPer; k++) {
+            const int j = jb + 8 * k, m = mc + j;
+            if (j >= cols || m >= p.M) continue;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                if (n0 + nc + 2 * q >= p.N) continue;  // the pair's gate row lies past N
+                const float gg = Elem<T>::load(sv[k].e[2 * q]);
+                const float uu = Elem<T>::load(sv[k].e[2 * q + 1]);
+                stf(out, (size_t)m * p.ldo + g0 + q, __fdiv_rn(__fmul_rn(uu, gg), __fadd_rn(1.0f, expf(-gg))));
             }
         }
     } else {
+        // RoPE + K/V append: four row pairs per piece
         const int half = p.dh >> 1;
         const int P = (p.nh + p.nkvh) * half;
+        const int g0 = (n0 + nc) >> 1;
+        int64_t pos[kPer];
 #pragma unroll
-        for (int h0 = 0; h0 < 32; h0 += 16) {
-            int64_t pos[16];
-            float2 cs[16];
+        for (int k = 0; k < kPer; k++) {
+            const int j = jb + 8 * k, m = mc + j;
+            pos[k] = j < cols && m < p.M ? ld_s64_early(p.pos + m) : 0;
+        }
+        float2 cs[kPer][4];
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-                const int m = mc + h0 + j;
-                pos[j] = h0 + j < cols && m < p.M ? p.pos[m] : 0;
+        for (int k = 0; k < kPer; k++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                cs[k][q] = make_float2(0.f, 0.f);
+                const int g = g0 + q;
+                if (g < P && pos[k] >= 0 && pos[k] < p.maxseq)
+                    cs[k][q] = ld_f2_early(p.table + (size_t)pos[k] * half + (g % half));
             }
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-                cs[j] = make_float2(0.f, 0.f);
-                if (g < P && h0 + j < cols && pos[j] >= 0 && pos[j] < p.maxseq)
-                    cs[j] = p.table[(size_t)pos[j] * half + (g % half)];
-            }
+        for (int k = 0; k < kPer; k++) {
+            const int j = jb + 8 * k, m = mc + j;
+            if (j >= cols || m >= p.M) continue;
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-                const int m = mc + h0 + j;
-                if (h0 + j < cols && m < p.M)
-                    rope_kv_store<T>(p, g, r1ok, m, v[h0 + j] + b0, pv[h0 + j] + b1, pos[j], cs[j]);
+            for (int q = 0; q < 4; q++) {
+                const int r0 = n0 + nc + 2 * q;
+                if (r0 >= p.N) continue;
+                rope_kv_store<T>(p, g0 + q, r0 + 1 < p.N, m, Elem<T>::load(sv[k].e[2 * q]),
+                                 Elem<T>::load(sv[k].e[2 * q + 1]), pos[k], cs[k][q]);
             }
         }
     }
@@ -273,16 +344,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = s_tmem;
     pdl_trigger();
-    pdl_wait();  // X (and, for residuals, the output) come from the previous kernel
 
     if (warp == 0) {
         if (lane == 0) {
-            // producer: TMA slices of W (128 rows) and X (tn rows) into the ring
+            // producer: TMA slices of W (128 rows) and X (tn rows) into the
+            // ring. The weights of the first stages do not depend on the
+            // previous kernel: they are requested before the wait for it;
+            // X (written by it) right after.
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tmW) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tmX) : "memory");
+            int pre = 0, m0f = 0, kbf = 0;
+            if ((int)blockIdx.x < sc.nunits) {
+                int t, n0, nk;
+                sc.unit(blockIdx.x, tn, t, n0, m0f, kbf, nk);
+                pre = min(nk, nst);
+                for (int kt = 0; kt < pre; kt++) {
+                    mb_expect_tx(&full[kt], (unsigned)st_bytes);
+                    tma_load_2d(smem + (size_t)kt * st_bytes, &tmW, (kbf + kt) * kBK, n0, &full[kt]);
+                }
+            }
+            pdl_wait();
+            for (int kt = 0; kt < pre; kt++)
+                tma_load_2d(smem + (size_t)kt * st_bytes + a_bytes, &tmX, (kbf + kt) * kBK, m0f, &full[kt]);
+            s_issued = pre;
             int it = 0;
             for (int u = blockIdx.x; u < sc.nunits; u += gridDim.x) {
                 int t, n0, m0, kb, nk;
                 sc.unit(u, tn, t, n0, m0, kb, nk);
                 for (int kt = 0; kt < nk; kt++, it++) {
+                    if (it < pre) continue;  // issued above
                     const int st = it % nst;
                     if (it >= nst && !mb_wait(&empty[st], (unsigned)(((it / nst) - 1) & 1))) {
                         atomicExch(&s_bad, 1);
@@ -298,6 +388,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
     } else if (warp == 1) {
+        // (reads only shared memory that the producer fills after its wait)
         if (lane == 0) {
             // MMA issuer
             const uint32_t idesc = idesc_bf16(tn);
@@ -334,8 +425,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // epilogue warps
+        pdl_wait();  // residuals (and the output) come from earlier kernels
         const int q = warp & 3;  // TMEM lane quarter
         const int row = q * 32 + lane;
+        const int et = threadIdx.x - 64;  // 0 .. 127 among the epilogue threads
+        __nv_bfloat16 *S = reinterpret_cast<__nv_bfloat16 *>(smem + (size_t)nst * st_bytes);
         const bool leader = warp == 2 && lane == 0;
         int i = 0;
         for (int u = blockIdx.x; u < sc.nunits; u += gridDim.x, i++) {
@@ -353,11 +447,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)buf * ncols;
             const int n = n0 + row;
-            float b0 = 0.f, b1 = 0.f;  // the row pair's bias, loaded once per unit
-            if (p.bias && (lane & 1) == 0 && n < p.N) {
-                b0 = ldf(reinterpret_cast<const T *>(p.bias), n);
-                if (n + 1 < p.N) b1 = ldf(reinterpret_cast<const T *>(p.bias), n + 1);
-            }
+            // this weight row's bias, loaded once per unit
+            const float brow = p.bias && n < p.N ? ldf(reinterpret_cast<const T *>(p.bias), n) : 0.f;
             if (sc.ksplit > 1) {
                 // split-K: add this unit's partial tile into the tile's f32
                 // accumulator ([tn][128], lanes contiguous; reductions in L2);
@@ -387,11 +478,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         float v[32];
 #pragma unroll
                         for (int j = 0; j < 32; j++)
-                            v[j] = c0 + j < tn ? __ldcg(ws + (size_t)(c0 + j) * 128 + row) : 0.f;
+                            v[j] = c0 + j < tn ? ld_f32_early(ws + (size_t)(c0 + j) * 128 + row) : 0.f;
+                        tc_epi_stage(S, row, v, brow);
+                        epi_bar();
+                        tc_epi_emit<EPI>(p, S, n0, m0 + c0, min(32, tn - c0), et);
 #pragma unroll
                         for (int j = 0; j < 32; j++)
                             if (c0 + j < tn) __stcg(ws + (size_t)(c0 + j) * 128 + row, 0.f);
-                        tc_epilogue<EPI>(p, n, m0 + c0, min(32, tn - c0), v, b0, b1);
+                        epi_bar();  // S is rewritten by the next chunk
                     }
                     if (leader) p.tc_cnt[t] = 0;
                 }
@@ -408,7 +502,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         __syncwarp();
                         if (lane == 0) mb_arrive(&acc_empty[buf]);
                     }
-                    tc_epilogue<EPI>(p, n, m0 + c0, min(32, tn - c0), v, b0, b1);
+                    tc_epi_stage(S, row, v, brow);
+                    epi_bar();
+                    tc_epi_emit<EPI>(p, S, n0, m0 + c0, min(32, tn - c0), et);
+                    epi_bar();  // S is rewritten by the next chunk
                 }
             }
         }
