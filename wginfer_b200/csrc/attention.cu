@@ -765,13 +765,14 @@ int launch_mma_attn(T *out, const T *q, KvDense<T> src, const AttnShape &sh, cud
 // heads that share the kv head are the 16 rows of an m16n8k16 A tile (rows
 // past hpc are zero), so every K/V row is read once per kv head and feeds
 // hpc query heads through mma.sync. Four warps split the CTA's keys; each
-// streams its own 32-key K/V tiles through a double-buffered shared-memory
+// streams its own 16-key K/V tiles through a double-buffered shared-memory
 // stage (cp.async), keeps a running max/sum per row and O += P V in
 // registers. The warps fold in shared memory, then the CTAs of the cluster
 // (the key slices) fold in CTA 0 through distributed shared memory.
 // Roofline: HBM, 2 * B * L * nkvh * d * size bytes of K/V.
 constexpr int kDW = 4;        // warps per CTA
-constexpr int kDK = 32;       // keys per warp tile
+constexpr int kDK = 16;       // keys per warp tile (small enough for two CTAs per SM)
+constexpr int kDN = kDK / 8;  // n-tiles of 8 keys per warp tile
 
 template <typename T, int DH> struct MmaDecLayout {
     static constexpr int RS = DH + 8;
@@ -779,8 +780,8 @@ template <typename T, int DH> struct MmaDecLayout {
     static constexpr size_t warp_stage = 4 * tile;                    // K, V x 2 buffers
     static constexpr size_t qs = 0;                                   // [16][RS] T
     static constexpr size_t kv = ((size_t)16 * RS * sizeof(T) + 127) & ~(size_t)127;
-    static constexpr size_t xo = kv + kDW * warp_stage;               // rank 0: [ns][16][DH] f32
-    static constexpr size_t bytes(int ns) { return xo + (size_t)ns * 16 * DH * 4; }
+    static constexpr size_t xo = kv + kDW * warp_stage;               // rank 0: [ns][hpc][DH] f32
+    static constexpr size_t bytes(int ns, int hpc) { return xo + (size_t)ns * hpc * DH * 4; }
 };
 
 template <typename T, int DH>
@@ -854,13 +855,13 @@ __global__ void __launch_bounds__(kDW * 32) attn_mma_decode_kernel(const T *__re
         __pipeline_wait_prior(1);
         __syncwarp();
         const T *kt = kbuf + (t & 1) * kDK * RS, *vt = vbuf + (t & 1) * kDK * RS;
-        float s[4][4];
+        float s[kDN][4];
 #pragma unroll
-        for (int n = 0; n < 4; n++) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+        for (int n = 0; n < kDN; n++) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
         for (int kk = 0; kk < NKS; kk++) {
 #pragma unroll
-            for (int n = 0; n < 4; n += 2) {
+            for (int n = 0; n < kDN; n += 2) {
                 uint32_t bb[4];
                 ldsm4(bb, kt + (n * 8 + (lane & 7) + (lane >> 4) * 8) * RS + kk * 16 + ((lane >> 3) & 1) * 8);
                 mma16816<T>(s[n], qf[kk], bb[0], bb[1]);
@@ -869,7 +870,7 @@ __global__ void __launch_bounds__(kDW * 32) attn_mma_decode_kernel(const T *__re
         }
         float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-        for (int n = 0; n < 4; n++) {
+        for (int n = 0; n < kDN; n++) {
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 const int j = w0 + t * kDK + n * 8 + 2 * t4 + (c & 1);
@@ -896,7 +897,7 @@ __global__ void __launch_bounds__(kDW * 32) attn_mma_decode_kernel(const T *__re
             o[i][3] *= corr[1];
         }
 #pragma unroll
-        for (int n = 0; n < 4; n++) {
+        for (int n = 0; n < kDN; n++) {
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 const float m = mrow[c >> 1];
@@ -949,7 +950,7 @@ __global__ void __launch_bounds__(kDW * 32) attn_mma_decode_kernel(const T *__re
     // fold the warps into this CTA's slice and push it to CTA 0 of the cluster
     float *xo0 = cluster.map_shared_rank(xo, 0);
     float *xm0 = cluster.map_shared_rank(&xm[0][0], 0), *xl0 = cluster.map_shared_rank(&xl[0][0], 0);
-    for (int x = tid; x < 16 * DH; x += kDW * 32) {
+    for (int x = tid; x < hpc * DH; x += kDW * 32) {
         const int row = x / DH, col = x - row * DH;
         float M = -INFINITY;
 #pragma unroll
@@ -965,7 +966,7 @@ __global__ void __launch_bounds__(kDW * 32) attn_mma_decode_kernel(const T *__re
                 }
             }
         }
-        xo0[((size_t)rank * 16 + row) * DH + col] = O;
+        xo0[((size_t)rank * hpc + row) * DH + col] = O;
         if (col == 0) {
             xm0[rank * 16 + row] = M;
             xl0[rank * 16 + row] = L;
@@ -983,7 +984,7 @@ __global__ void __launch_bounds__(kDW * 32) attn_mma_decode_kernel(const T *__re
                     if (xl[r][row] > 0.f) {
                         const float e = ex2(xm[r][row] - MM);
                         LL += xl[r][row] * e;
-                        OO += xo[((size_t)r * 16 + row) * DH + col] * e;
+                        OO += xo[((size_t)r * hpc + row) * DH + col] * e;
                     }
                 }
             }
@@ -1003,7 +1004,7 @@ int launch_mma_decode(T *out, const T *q, KvCache<T> src, const AttnShape &sh, c
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ns, (unsigned)(sh.S * sh.nkvh), 1);
     cfg.blockDim = dim3(kDW * 32, 1, 1);
-    cfg.dynamicSmemBytes = MmaDecLayout<T, DH>::bytes(ns);
+    cfg.dynamicSmemBytes = MmaDecLayout<T, DH>::bytes(ns, sh.nh / sh.nkvh);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1168,9 +1169,9 @@ template <typename T, class Src> void set_attrs() {
     cudaFuncSetAttribute(attn_fast_kernel<T, Src, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if constexpr (sizeof(T) == 2 && IsKvCache<Src>::value) {
         cudaFuncSetAttribute(attn_mma_decode_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)MmaDecLayout<T, 128>::bytes(kMaxCluster));
+                             (int)MmaDecLayout<T, 128>::bytes(kMaxCluster, 16));
         cudaFuncSetAttribute(attn_mma_decode_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)MmaDecLayout<T, 64>::bytes(kMaxCluster));
+                             (int)MmaDecLayout<T, 64>::bytes(kMaxCluster, 16));
     }
     if constexpr (sizeof(T) == 2) {
         cudaFuncSetAttribute(attn_mma_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
