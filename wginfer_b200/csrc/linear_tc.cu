@@ -170,6 +170,8 @@ __device__ __forceinline__ float2 ld_f2_early(const float2 *p) {
 //          requested before its first store.
 // (A thread that walked its 32 input rows itself issued scattered 2-byte
 // accesses one row at a time; that cost one memory round trip per row.)
+// The RoPE piece hoists everything that depends only on the weight rows
+// (head, rotation index, q/k/v) out of the loop over input rows.
 
 __device__ __forceinline__ void tc_epi_stage(__nv_bfloat16 *S, int row, const float (&v)[32], float b) {
 #pragma unroll
@@ -243,36 +245,81 @@ __device__ __forceinline__ void tc_epi_emit(const DecodeGemvParams &p, const __n
             }
         }
     } else {
-        // RoPE + K/V append: four row pairs per piece
+        // RoPE + K/V append. A piece is four row pairs g0 .. g0 + 3 of one
+        // head (q or k: rotation partners (jj, jj + dh/2), jj = g0 % (dh/2) ..
+        // + 3) or eight consecutive v values; per input row: its position,
+        // four {cos, sin} (32 bytes) and two 8-byte stores (q, k) or one
+        // 16-byte store (v).
         const int half = p.dh >> 1;
         const int P = (p.nh + p.nkvh) * half;
         const int g0 = (n0 + nc) >> 1;
+        const bool qk = g0 < P;
+        const int h = g0 / half, jj0 = g0 - h * half, e0 = 2 * (g0 - P);
+        const bool vec = n0 + nc + 8 <= p.N && (half & 3) == 0 && (p.dh & 7) == 0 && (P & 3) == 0 &&
+                         ((uintptr_t)p.q_out & 15) == 0 && ((uintptr_t)p.kc & 15) == 0 &&
+                         ((uintptr_t)p.vc & 15) == 0 && ((uintptr_t)p.table & 15) == 0 && (p.seq_stride & 7) == 0;
         int64_t pos[kPer];
 #pragma unroll
         for (int k = 0; k < kPer; k++) {
             const int j = jb + 8 * k, m = mc + j;
-            pos[k] = j < cols && m < p.M ? ld_s64_early(p.pos + m) : 0;
+            pos[k] = j < cols && m < p.M ? ld_s64_early(p.pos + m) : -1;
         }
-        float2 cs[kPer][4];
+        if (!vec) {  // ragged or unaligned: one pair at a time
 #pragma unroll
-        for (int k = 0; k < kPer; k++)
+            for (int k = 0; k < kPer; k++) {
+                const int j = jb + 8 * k, m = mc + j;
+                if (j >= cols || m >= p.M) continue;
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                cs[k][q] = make_float2(0.f, 0.f);
-                const int g = g0 + q;
-                if (g < P && pos[k] >= 0 && pos[k] < p.maxseq)
-                    cs[k][q] = ld_f2_early(p.table + (size_t)pos[k] * half + (g % half));
+                for (int q = 0; q < 4; q++) {
+                    const int r0 = n0 + nc + 2 * q, g = g0 + q;
+                    if (r0 >= p.N) continue;
+                    float2 cs = make_float2(0.f, 0.f);
+                    if (g < P && pos[k] >= 0 && pos[k] < p.maxseq) cs = p.table[(size_t)pos[k] * half + (g % half)];
+                    rope_kv_store<T>(p, g, r0 + 1 < p.N, m, Elem<T>::load(sv[k].e[2 * q]),
+                                     Elem<T>::load(sv[k].e[2 * q + 1]), pos[k], cs);
+                }
             }
+            return;
+        }
+        float4 cs[kPer][2];
+#pragma unroll
+        for (int k = 0; k < kPer; k++) {
+            cs[k][0] = cs[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (qk && pos[k] >= 0 && pos[k] < p.maxseq) {
+                const float2 *c = p.table + (size_t)pos[k] * half + jj0;
+                const uint4 a = ld_global_v4_early(c), b = ld_global_v4_early(c + 2);
+                cs[k][0] = make_float4(__uint_as_float(a.x), __uint_as_float(a.y), __uint_as_float(a.z),
+                                       __uint_as_float(a.w));
+                cs[k][1] = make_float4(__uint_as_float(b.x), __uint_as_float(b.y), __uint_as_float(b.z),
+                                       __uint_as_float(b.w));
+            }
+        }
 #pragma unroll
         for (int k = 0; k < kPer; k++) {
             const int j = jb + 8 * k, m = mc + j;
             if (j >= cols || m >= p.M) continue;
+            if (pos[k] < 0 || pos[k] >= p.maxseq) {
+                record_device_error(p.err, 3, pos[k]);
+                continue;
+            }
+            const int seq = p.prefill_seq >= 0 ? p.prefill_seq : m;
+            const size_t cache = (size_t)seq * p.seq_stride + (size_t)pos[k] * p.nkvh * p.dh;
+            if (qk) {
+                T *dst = h < p.nh ? reinterpret_cast<T *>(p.q_out) + ((size_t)m * p.nh + h) * p.dh
+                                  : reinterpret_cast<T *>(p.kc) + cache + (size_t)(h - p.nh) * p.dh;
+                const float c4[4] = {cs[k][0].x, cs[k][0].z, cs[k][1].x, cs[k][1].z};
+                const float s4[4] = {cs[k][0].y, cs[k][0].w, cs[k][1].y, cs[k][1].w};
+                union { uint2 u; T e[4]; } lo, hi;
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const int r0 = n0 + nc + 2 * q;
-                if (r0 >= p.N) continue;
-                rope_kv_store<T>(p, g0 + q, r0 + 1 < p.N, m, Elem<T>::load(sv[k].e[2 * q]),
-                                 Elem<T>::load(sv[k].e[2 * q + 1]), pos[k], cs[k][q]);
+                for (int q = 0; q < 4; q++) {
+                    const float a = Elem<T>::load(sv[k].e[2 * q]), b = Elem<T>::load(sv[k].e[2 * q + 1]);
+                    lo.e[q] = Elem<T>::store(__fsub_rn(__fmul_rn(a, c4[q]), __fmul_rn(b, s4[q])));
+                    hi.e[q] = Elem<T>::store(__fadd_rn(__fmul_rn(a, s4[q]), __fmul_rn(b, c4[q])));
+                }
+                *reinterpret_cast<uint2 *>(dst + jj0) = lo.u;
+                *reinterpret_cast<uint2 *>(dst + jj0 + half) = hi.u;
+            } else {
+                *reinterpret_cast<uint4 *>(reinterpret_cast<T *>(p.vc) + cache + e0) = sv[k].u;
             }
         }
     }
