@@ -373,10 +373,10 @@ def run_b200(args):
         "e2e": {"value": round(world * K / te, 2), "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
         "roofline": roof,
         "clocks": clk.summary(),
-        # per step: decode_begin, embedding, 28 x (qkv gemv [rms, rope, kv append fused], attention,
+        # per step: embedding, 28 x (qkv gemv [rms, rope, kv append fused], attention,
         # o gemv [+residual], gate/up gemv [rms, swiglu fused], down gemv [+residual]), lm_head gemv
         # [final rms fused], argmax, decode_end
-        "gpu_launches": K * (2 + 28 * 5 + 3),
+        "gpu_launches": K * (1 + 28 * 5 + 3),
     })
     if not args.no_bs64:
         result["bs64"] = bs64(args, world, rank, local)

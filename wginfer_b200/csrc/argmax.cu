@@ -28,7 +28,10 @@ namespace {
 
 constexpr int kCluster = 8;
 constexpr int kThreads = 256;
-constexpr int kB = 4;  // 16-byte vectors in flight per thread
+// 16-byte vectors in flight per thread: 4 when the rows fill the GPU; 10 for
+// a few rows, where a 151936-wide bf16 row on 8 CTAs is then one round trip
+// (latency, not bandwidth, is what a few rows pay for)
+constexpr int kBWide = 4, kBFew = 10;
 
 __device__ __forceinline__ unsigned long long make_key(float v, uint32_t idx) {
     if (v == 0.f) v = 0.f;  // -0 -> +0
@@ -69,8 +72,8 @@ template <> __device__ __forceinline__ float vec_max<float>(const Vec16<float> &
     return fmaxf(fmaxf(r.e[0], r.e[1]), fmaxf(r.e[2], r.e[3]));
 }
 
-template <typename T, bool kVec>
-__global__ void __launch_bounds__(kThreads, 4) argmax_cluster_kernel(int64_t *max_idx, T *max_val, const T *vals,
+template <typename T, bool kVec, int kB>
+__global__ void __launch_bounds__(kThreads, kB > 4 ? 2 : 4) argmax_cluster_kernel(int64_t *max_idx, T *max_val, const T *vals,
                                                                   size_t numel) {
     constexpr int V = Vec16<T>::N;
     __shared__ unsigned long long red[kThreads / 32];
@@ -170,14 +173,16 @@ int launch_argmax(int64_t *idx, T *val, const T *vals, size_t rows, size_t numel
     int per_sm = dev >= 0 && dev < 64 ? resident[dev][vec ? 1 : 0].load(std::memory_order_relaxed) : 0;
     if (per_sm <= 0) {
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                &per_sm, vec ? argmax_cluster_kernel<T, true> : argmax_cluster_kernel<T, false>, kThreads, 0) !=
-                cudaSuccess ||
+                &per_sm, vec ? argmax_cluster_kernel<T, true, kBWide> : argmax_cluster_kernel<T, false, kBWide>,
+                kThreads, 0) != cudaSuccess ||
             per_sm < 1) {
             cudaGetLastError();
             per_sm = 1;
         }
         if (dev >= 0 && dev < 64) resident[dev][vec ? 1 : 0].store(per_sm, std::memory_order_relaxed);
     }
+    // few rows (every row gets the full cluster): the deeper batch
+    const bool few = rows * kCluster <= (size_t)sm_count();
     const size_t wave = (size_t)sm_count() * per_sm;
     size_t ns = rows >= wave ? 1 : wave / rows;
     if (ns > (size_t)kCluster) ns = kCluster;
@@ -193,8 +198,10 @@ int launch_argmax(int64_t *idx, T *val, const T *vals, size_t rows, size_t numel
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true>, idx, val, vals, numel)
-                        : cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, false>, idx, val, vals, numel);
+    cudaError_t e;
+    if (vec && few) e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true, kBFew>, idx, val, vals, numel);
+    else if (vec) e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true, kBWide>, idx, val, vals, numel);
+    else e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, false, kBWide>, idx, val, vals, numel);
     if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "wgb_argmax: %s", cudaGetErrorString(e));
     return check_launch("wgb_argmax");
 }

@@ -29,7 +29,19 @@ __global__ void __launch_bounds__(256) embedding_kernel(char *out, const int64_t
             continue;
         }
         const W *src = reinterpret_cast<const W *>(weight) + (size_t)id * row_words;
-        for (size_t k = lane; k < row_words; k += 32) dst[k] = src[k];
+        // up to 8 words per lane are requested before the first store (a
+        // store may alias a later load, so a load-store loop would wait
+        // for every word in turn)
+        constexpr int kU = 8;
+        for (size_t k0 = lane; k0 < row_words; k0 += 32 * kU) {
+            W r[kU];
+#pragma unroll
+            for (int u = 0; u < kU; u++)
+                if (k0 + 32 * u < row_words) r[u] = src[k0 + 32 * u];
+#pragma unroll
+            for (int u = 0; u < kU; u++)
+                if (k0 + 32 * u < row_words) dst[k0 + 32 * u] = r[u];
+        }
     }
 }
 

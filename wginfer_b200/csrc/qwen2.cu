@@ -111,11 +111,6 @@ __global__ void fill_positions_kernel(int64_t *pos, int64_t start, int n) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) pos[i] = start + i;
 }
 
-__global__ void decode_begin_kernel(int64_t *pos, const int64_t *lens, int B) {
-    const int b = blockIdx.x * blockDim.x + threadIdx.x;
-    if (b < B) pos[b] = lens[b];
-}
-
 __global__ void decode_end_kernel(int64_t *lens, int B, int maxseq) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b < B && lens[b] < maxseq) lens[b] += 1;
@@ -273,6 +268,11 @@ int attention(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t total_l
                        (int)m.nkvh, (int)m.dh, (int)m.maxseq, scale, M->attn_ws, ref, s, pf_ptr, pf_bytes);
 }
 
+// Positions of the layer's rows: the prefill chunk's (filled per chunk), or,
+// in batched decode, each sequence's current length (row b's new token sits
+// at lens[b]; decode_end advances lens after the step).
+const int64_t *positions(const wgbQwen2Model *M, int prefill_seq) { return prefill_seq >= 0 ? M->pos : M->lens; }
+
 // One transformer layer over T rows (model.cpp:243-328), REFERENCE numerics:
 // the reference's op sequence with each op in the reference summation order.
 int run_layer_ref(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t total_len) {
@@ -290,7 +290,7 @@ int run_layer_ref(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t tot
         dim3 grid((unsigned)((work + 127) / 128), (unsigned)T);
         WGB_DISPATCH_FLOAT(M->dt, Tt,
             qkv_post_kernel<Tt><<<grid, 128, 0, s>>>((const Tt *)M->qkv, (Tt *)M->qr, (Tt *)M->layer_k(l),
-                                                     (Tt *)M->layer_v(l), M->pos, M->rope_table, T, (int)m.nh,
+                                                     (Tt *)M->layer_v(l), positions(M, prefill_seq), M->rope_table, T, (int)m.nh,
                                                      (int)m.nkvh, (int)m.dh, (int)m.maxseq, prefill_seq,
                                                      M->seq_stride, dev_error_ptr()));
         if ((rc = cuda_err("qkv_post"))) return rc;
@@ -348,7 +348,7 @@ int run_layer_fast(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t to
     p.groups = (int)((m.nh + m.nkvh) * half + m.nkvh * m.dh / 2);
     p.norm_w = w.attn_norm;
     p.bias = w.qkv_b;
-    p.pos = M->pos;
+    p.pos = positions(M, prefill_seq);
     p.table = M->rope_table;
     p.q_out = M->qr;
     p.kc = M->layer_k(l);
@@ -462,8 +462,6 @@ int decode_body(wgbQwen2Model *M, int B, bool ref) {
     cudaStream_t s = M->stream;
     int rc;
 
-    decode_begin_kernel<<<(B + 127) / 128, 128, 0, s>>>(M->pos, M->lens, B);
-    WGB_TRACE("decode_begin");
     if ((rc = wgb_embedding(M->x, M->tokens, M->in_embed, M->dt, B, m.hs, m.voc, s))) return rc;
     WGB_TRACE("embedding");
     for (size_t l = 0; l < m.nlayer; l++)
