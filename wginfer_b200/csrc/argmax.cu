@@ -81,6 +81,10 @@ __global__ void __launch_bounds__(kThreads, kB > 4 ? 2 : 4) argmax_cluster_kerne
     const unsigned rank = cluster.block_rank(), ns = cluster.num_blocks();
     const size_t row = blockIdx.x / ns;
     const T *x = vals + row * numel;
+    // launched with programmatic dependent launch: this CTA may start while
+    // the kernel that writes `vals` finishes; it waits for it before reading
+    pdl_trigger();
+    pdl_wait();
     Best bt{-INFINITY, 0xFFFFFFFFu};
 
     if (kVec) {
@@ -191,13 +195,15 @@ int launch_argmax(int64_t *idx, T *val, const T *vals, size_t rows, size_t numel
     cfg.gridDim = dim3((unsigned)(rows * ns));
     cfg.blockDim = dim3(kThreads);
     cfg.stream = s;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = (unsigned)ns;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     cudaError_t e;
     if (vec && few) e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true, kBFew>, idx, val, vals, numel);
     else if (vec) e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true, kBWide>, idx, val, vals, numel);

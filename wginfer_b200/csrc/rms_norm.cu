@@ -67,11 +67,11 @@ __global__ void __launch_bounds__(256) rms_warp_kernel(T *__restrict__ out, cons
     }
 }
 
-template <typename T, int VPT>
-__global__ void __launch_bounds__(256) rms_block_kernel(T *__restrict__ out, const T *__restrict__ in,
-                                                        const T *__restrict__ w, int M, int N, float eps) {
+template <typename T, int VPT, int NT>
+__global__ void __launch_bounds__(NT) rms_block_kernel(T *__restrict__ out, const T *__restrict__ in,
+                                                       const T *__restrict__ w, int M, int N, float eps) {
     constexpr int V = Vec16<T>::N;
-    __shared__ float red[8];
+    __shared__ float red[NT / 32];
     const int row = blockIdx.x;
     const int nvec = N / V;
     const T *x = in + (size_t)row * N;
@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(256) rms_block_kernel(T *__restrict__ out, con
     float ss = 0.f;
 #pragma unroll
     for (int u = 0; u < VPT; u++) {  // x and the norm weight in one round trip
-        int vi = threadIdx.x + u * 256;
+        int vi = threadIdx.x + u * NT;
         if (vi < nvec) {
             r[u].u = ld_global_nc_v4(x + (size_t)vi * V);
             wr[u].u = ld_global_l1_v4(w + (size_t)vi * V);  // every row reads w: keep it in L1
@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(256) rms_block_kernel(T *__restrict__ out, con
     }
 #pragma unroll
     for (int u = 0; u < VPT; u++) {
-        int vi = threadIdx.x + u * 256;
+        int vi = threadIdx.x + u * NT;
         if (vi < nvec) {
 #pragma unroll
             for (int e = 0; e < V; e++) {
@@ -99,13 +99,13 @@ __global__ void __launch_bounds__(256) rms_block_kernel(T *__restrict__ out, con
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
-    float tot = (threadIdx.x & 31) < 8 ? red[threadIdx.x & 31] : 0.f;
+    float tot = (threadIdx.x & 31) < NT / 32 ? red[threadIdx.x & 31] : 0.f;
     tot = warp_sum(tot);
     const float sc = rms_scale(tot, N, eps);
     T *y = out + (size_t)row * N;
 #pragma unroll
     for (int u = 0; u < VPT; u++) {
-        int vi = threadIdx.x + u * 256;
+        int vi = threadIdx.x + u * NT;
         if (vi < nvec) {
             Vec16<T> o;
 #pragma unroll
@@ -192,9 +192,12 @@ int launch_rms(T *out, const T *in, const T *w, size_t M, size_t N, float eps, c
         else if (nvec <= 32 * 6) rms_warp_kernel<T, 6><<<blocks, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
         else rms_warp_kernel<T, 8><<<blocks, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
     } else if (vec_ok && nvec <= 256 * 8) {
-        if (nvec <= 256 * 2) rms_block_kernel<T, 2><<<(int)M, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
-        else if (nvec <= 256 * 4) rms_block_kernel<T, 4><<<(int)M, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
-        else rms_block_kernel<T, 8><<<(int)M, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
+        // up to 4 vectors of the row (and 4 of the weight) per thread: the
+        // longest rows take 512 threads rather than 8 vectors a thread,
+        // which halved the CTAs resident per SM
+        if (nvec <= 256 * 2) rms_block_kernel<T, 2, 256><<<(int)M, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
+        else if (nvec <= 256 * 4) rms_block_kernel<T, 4, 256><<<(int)M, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
+        else rms_block_kernel<T, 4, 512><<<(int)M, 512, 0, s>>>(out, in, w, (int)M, (int)N, eps);
     } else {
         int blocks = (int)(M < (size_t)grid_cap ? M : grid_cap);
         rms_generic_kernel<T><<<blocks, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
