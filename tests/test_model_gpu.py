@@ -66,8 +66,11 @@ def test_full_model_stream_reference_numerics(cuda, name):
     assert toks == gold, f"first divergence at step {first}"
 
 
-@pytest.mark.parametrize("name", ["tiny_p16_g64", "one_layer_p16_g12", "qwen2_1p5b_p16_g128"])
+@pytest.mark.parametrize("name", ["tiny_p16_g64", "tiny_p100_g32", "one_layer_p16_g12", "qwen2_1p5b_p16_g128",
+                                  "qwen2_1p5b_p512_g128"])
 def test_stream_fast_numerics_teacher_forced(cuda, name):
+    """(The 512-token prompt runs its projections on the tensor cores with
+    256-row input tiles and K split across CTAs.)"""
     if name not in STREAMS:
         pytest.skip(f"golden stream {name} not generated")
     spec = CS.SMALL_MODELS.get(name) or CS.FULL_MODELS[name][:3]

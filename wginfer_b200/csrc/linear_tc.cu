@@ -630,9 +630,11 @@ int pick_tn(int M, int N) {
     return tn;
 }
 
-// Split-K plan for up to 64 input rows: when the weight tiles cannot fill
-// half the SMs, keep the widest input tile (the weights are read once) and
-// split K across CTAs instead, as many splits as fit in one wave; the
+// Split-K plan: when the weight tiles of the widest input tile (up to 256
+// rows) cannot fill half the SMs (q/k/v, o and down at batch 64 or in a
+// 512-token prefill chunk), keep that tile (the weights are read once, and
+// wide MMAs) and split K across CTAs instead, as many splits as fit in one
+// wave; the
 // partial sums meet in an f32 accumulator in L2 (tc_ws, one [tn][128] tile
 // per output tile, zero between launches). The order in which the splits
 // add up varies from run to run (FAST numerics: f32 sums in any order).
@@ -645,7 +647,7 @@ void plan_split(const DecodeGemvParams &p, int &tn, int &ksplit, int &kper) {
     while (wide < p.M && wide < 256) wide *= 2;
     const long long tiles = (long long)((p.N + kTileW - 1) / kTileW) * ((p.M + wide - 1) / wide);
     const long long sms = sm_count();
-    if (p.tc_ws && p.tc_cnt && wide <= 64 && 2 * tiles <= sms && tiles <= p.tc_cnt_n && ktiles >= 2 &&
+    if (p.tc_ws && p.tc_cnt && 2 * tiles <= sms && tiles <= p.tc_cnt_n && ktiles >= 2 &&
         (size_t)tiles * 128 * wide * sizeof(float) <= p.tc_ws_bytes) {
         int ks = (int)(sms / tiles);
         if (ks > ktiles) ks = ktiles;
