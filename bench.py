@@ -507,6 +507,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--numerics", default="fast", choices=["fast", "reference"])
     ap.add_argument("--no-bs64", action="store_true")
+    ap.add_argument("--only-bs64", action="store_true",
+                    help="print only the batched-decode result (64 sequences x 2048-token prompts)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the elementwise/reduction bandwidth sweep")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
@@ -516,6 +518,14 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.only_bs64:
+        world, rank, local = dist_setup(args.gpus)
+        r = bs64(args, world, rank, local)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "unit": UNIT, "n_gpus": world, "bs64": r}), flush=True)
     else:
         run_b200(args)
 
