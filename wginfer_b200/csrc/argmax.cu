@@ -28,10 +28,10 @@ namespace {
 
 constexpr int kCluster = 8;
 constexpr int kThreads = 256;
-// 16-byte vectors in flight per thread: 4 when the rows fill the GPU; 10 for
+// 16-byte vectors in flight per thread: 8 when the rows fill the GPU; 10 for
 // a few rows, where a 151936-wide bf16 row on 8 CTAs is then one round trip
 // (latency, not bandwidth, is what a few rows pay for)
-constexpr int kBWide = 4, kBFew = 10;
+constexpr int kBWide = 8, kBFew = 10;
 
 __device__ __forceinline__ unsigned long long make_key(float v, uint32_t idx) {
     if (v == 0.f) v = 0.f;  // -0 -> +0
@@ -73,7 +73,7 @@ template <> __device__ __forceinline__ float vec_max<float>(const Vec16<float> &
 }
 
 template <typename T, bool kVec, int kB>
-__global__ void __launch_bounds__(kThreads, kB > 4 ? 2 : 4) argmax_cluster_kernel(int64_t *max_idx, T *max_val, const T *vals,
+__global__ void __launch_bounds__(kThreads, kB > 8 ? 2 : 4) argmax_cluster_kernel(int64_t *max_idx, T *max_val, const T *vals,
                                                                   size_t numel) {
     constexpr int V = Vec16<T>::N;
     __shared__ unsigned long long red[kThreads / 32];
