@@ -151,11 +151,24 @@ def test_batched_decode_many_sequences_logits(cuda, cfg_name, B):
 
 
 def test_infer_sampling_path(cuda):
+    """Non-greedy infer samples on the device (wgb_sample_rows) with the
+    reference's rules: top_k = 1 is the argmax at any temperature, and a
+    top_k draw lies among the top_k logits."""
     m = model(CS.TINY)
     m.reset_cache()
-    t = m.infer(CS.prompt(8, CS.TINY.voc), top_k=50, top_p=0.9, temperature=0.7)
+    ids = CS.prompt(8, CS.TINY.voc)
+    t = m.infer(ids, top_k=50, top_p=0.9, temperature=0.7)
     assert 0 <= t < CS.TINY.voc
     assert m.cache_len() == 8
+    m.reset_cache()
+    greedy = m.infer(ids)
+    logits = m.logits(0).astype(np.float32)
+    m.reset_cache()
+    assert m.infer(ids, top_k=1, top_p=1.0, temperature=0.7) == greedy
+    top3 = set(np.argsort(-logits, kind="stable")[:3].tolist())
+    for _ in range(8):
+        m.reset_cache()
+        assert m.infer(ids, top_k=3, top_p=1.0, temperature=1.3) in top3
 
 
 def test_checkpoint_load_matches_direct_weights(cuda, tmp_path):

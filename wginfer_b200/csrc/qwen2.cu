@@ -21,7 +21,6 @@
 #include <cstdlib>
 #include <cstring>
 #include <algorithm>
-#include <numeric>
 #include <random>
 #include <string>
 #include <vector>
@@ -116,58 +115,6 @@ __global__ void decode_end_kernel(int64_t *lens, int B, int maxseq) {
     if (b < B && lens[b] < maxseq) lens[b] += 1;
 }
 
-int64_t argmax_host(const std::vector<float> &v) {
-    size_t best = 0;
-    for (size_t i = 1; i < v.size(); ++i)
-        if (v[i] > v[best]) best = i;
-    return (int64_t)best;
-}
-
-// Host sampling, the reference's sample_from_logits (model.cpp:60-137).
-int64_t sample_host(const std::vector<float> &logits, int top_k, float top_p, float temperature) {
-    if (temperature <= 0.0f) return argmax_host(logits);
-    const size_t vocab = logits.size();
-    if (top_k <= 0 || top_k > (int)vocab) top_k = (int)vocab;
-    if (top_p <= 0.0f || top_p > 1.0f) top_p = 1.0f;
-    if (top_k == 1 && top_p >= 1.0f) return argmax_host(logits);
-    std::vector<int> idx(vocab);
-    std::iota(idx.begin(), idx.end(), 0);
-    auto desc = [&logits](int a, int b) { return logits[a] > logits[b]; };
-    if (top_k < (int)vocab) {
-        std::partial_sort(idx.begin(), idx.begin() + top_k, idx.end(), desc);
-        idx.resize(top_k);
-    } else {
-        std::sort(idx.begin(), idx.end(), desc);
-    }
-    const float inv_t = 1.0f / temperature;
-    float mx = -INFINITY;
-    for (int i : idx) mx = std::max(mx, logits[i] * inv_t);
-    std::vector<double> probs(idx.size());
-    double total = 0.0;
-    for (size_t i = 0; i < idx.size(); ++i) {
-        double p = std::exp((double)(logits[idx[i]] * inv_t - mx));
-        if (!std::isfinite(p) || p < 0.0) p = 0.0;
-        probs[i] = p;
-        total += p;
-    }
-    if (total <= 0.0) return idx.front();
-    if (top_p < 1.0f) {
-        double cum = 0.0;
-        size_t keep = 0;
-        for (size_t i = 0; i < probs.size(); ++i) {
-            cum += probs[i] / total;
-            keep = i + 1;
-            if (cum >= (double)top_p) break;
-        }
-        keep = std::max<size_t>(keep, 1);
-        idx.resize(keep);
-        probs.resize(keep);
-    }
-    thread_local std::mt19937 rng(std::random_device{}());
-    std::discrete_distribution<int> dist(probs.begin(), probs.end());
-    return idx[(size_t)dist(rng)];
-}
-
 }  // namespace
 }  // namespace wgb
 
@@ -207,6 +154,7 @@ struct wgbQwen2Model {
     unsigned *tc_cnt;  // [kTcSites][kTcCounters] arrival counters (zero between launches)
     size_t attn_ws_bytes;
     int64_t *h_pinned;  // pinned host staging for token ids
+    unsigned long long sample_seed = 0, sample_step = 0;  // device sampler: seed, draws so far
     size_t h_pinned_n;
     std::vector<size_t> h_lens;
     std::vector<bool> has_bias;
@@ -638,6 +586,9 @@ int wgb_qwen2_create(const wgbQwen2Meta *meta, int device, int max_batch, wgbQwe
     }
     int rc = WGB_OK;
     if (cudaStreamCreateWithFlags(&M->stream, cudaStreamNonBlocking) != cudaSuccess) rc = cuda_err("stream");
+    // like the reference's sampler (model.cpp:131), seeded from the system's
+    // random device: draws differ between models and runs
+    M->sample_seed = ((unsigned long long)std::random_device{}() << 32) ^ std::random_device{}();
     // zero everything (biases default to zero, like the reference's dummy biases)
     if (!rc && cudaMemsetAsync(M->arena, 0, total, M->stream) != cudaSuccess) rc = cuda_err("arena memset");
     auto table = build_rope_table(m.maxseq, m.dh, m.theta);
@@ -793,31 +744,15 @@ int wgb_qwen2_infer(wgbQwen2Model *M, const int64_t *ids, size_t n, int top_k, f
         *next = M->h_pinned[0];
         return WGB_OK;
     }
-    const size_t V = M->m.voc;
-    std::vector<uint16_t> h16;
-    std::vector<float> lg(V);
-    if (M->dt == WGINFER_DTYPE_F32) {
-        if (cudaMemcpyAsync(lg.data(), M->logits, V * 4, cudaMemcpyDeviceToHost, M->stream) != cudaSuccess)
-            return cuda_err("logits D2H");
-    } else {
-        h16.resize(V);
-        if (cudaMemcpyAsync(h16.data(), M->logits, V * 2, cudaMemcpyDeviceToHost, M->stream) != cudaSuccess)
-            return cuda_err("logits D2H");
-    }
-    if (cudaStreamSynchronize(M->stream) != cudaSuccess) return cuda_err("logits sync");
-    if (M->dt == WGINFER_DTYPE_BF16) {
-        for (size_t i = 0; i < V; i++) {
-            uint32_t u = (uint32_t)h16[i] << 16;
-            memcpy(&lg[i], &u, 4);
-        }
-    } else if (M->dt == WGINFER_DTYPE_F16) {
-        for (size_t i = 0; i < V; i++) {
-            __half_raw r;
-            r.x = h16[i];
-            lg[i] = __half2float(__half(r));
-        }
-    }
-    *next = sample_host(lg, top_k, top_p, temperature);
+    // sampling (model.cpp:60-137) on the device: the logits stay there, only
+    // the drawn token comes back
+    if ((rc = wgb_sample_rows(M->tokens, M->logits, M->dt, 1, M->m.voc, top_k, top_p, temperature, M->sample_seed,
+                              M->sample_step++, M->stream)))
+        return rc;
+    if (cudaMemcpyAsync(M->h_pinned, M->tokens, sizeof(int64_t), cudaMemcpyDeviceToHost, M->stream) != cudaSuccess ||
+        cudaStreamSynchronize(M->stream) != cudaSuccess)
+        return cuda_err("infer D2H");
+    *next = M->h_pinned[0];
     return WGB_OK;
 }
 
