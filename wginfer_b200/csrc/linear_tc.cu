@@ -4,7 +4,7 @@
 // A work unit is 128 weight rows (the MMA's M dimension, one TMEM lane each)
 // x TN input rows (the MMA's N dimension, TN in {16, 32, 64, 128, 256}) x a
 // range of K; its f32 accumulator [128 x TN] lives in tensor memory. The
-// kernel is persistent (one CTA per SM, units strided over the grid) and
+// kernel is persistent (one or two CTAs per SM, units strided over the grid) and
 // warp-specialised: warp 0 streams 64-wide K slices of W and X into a
 // shared-memory ring with TMA (cp.async.bulk.tensor, 128-byte swizzle, no
 // multicast); one thread of warp 1 issues tcgen05.mma (kind::f16, bf16 in,
@@ -112,9 +112,14 @@ __host__ __device__ inline uint32_t idesc_bf16(int tn) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(tn >> 3) << 17) | ((uint32_t)(kTileW >> 4) << 24);
 }
 
-// Stages in the ring: as many as fit in about 192 KB (one CTA per SM), at
-// most kTcMaxStages: 8 for input tiles up to 64 rows, 6 for 128, 4 for 256.
+// CTAs per SM: two for input tiles up to 64 rows (their MMAs are narrow, and
+// a second CTA's MMA and TMA stream interleave with the first's: +5% at 64
+// rows of batched decode), else one.
+inline int tc_ctas_per_sm(int tn) { return tn <= 64 ? 2 : 1; }
+// Stages in the ring: 4 when two CTAs share an SM, else as many as fit in
+// about 192 KB, at most kTcMaxStages: 6 for 128 input rows, 4 for 256.
 inline int tc_stages(int tn) {
+    if (tc_ctas_per_sm(tn) > 1) return 4;
     const int st = kTileW * kBK * 2 + tn * kBK * 2;
     const int n = (192 * 1024) / st;
     return n > kTcMaxStages ? kTcMaxStages : n;
@@ -690,9 +695,10 @@ int launch_tc(const DecodeGemvParams &p, cudaStream_t s) {
         if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
     }
     cudaLaunchConfig_t cfg = {};
-    // persistent: one CTA per SM (its ring takes most of the shared memory),
-    // each taking units blockIdx.x, blockIdx.x + gridDim.x, ...
-    cfg.gridDim = dim3((unsigned)(sc.nunits < sm_count() ? sc.nunits : sm_count()));
+    // persistent: one or two CTAs per SM (the ring takes most of the shared
+    // memory), each taking units blockIdx.x, blockIdx.x + gridDim.x, ...
+    const int cap = sm_count() * tc_ctas_per_sm(tn);
+    cfg.gridDim = dim3((unsigned)(sc.nunits < cap ? sc.nunits : cap));
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = tc_smem_bytes(tn);
     cfg.stream = s;
