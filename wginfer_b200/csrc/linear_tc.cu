@@ -625,13 +625,14 @@ bool make_map(CUtensorMap *tm, const void *base, int rows, int K, int box_rows) 
 
 // Input rows per tile: the smallest power of two >= M up to 256 (the MMA's
 // largest N; fewer re-reads of the weight tile), then halved (down to 16)
-// only while the grid would leave more than half the SMs idle: each halving
+// only while the grid would leave more than half the CTA slots idle (two per
+// SM for tiles up to 64 rows): each halving
 // re-reads the weights once more (from L2) and makes every MMA narrower.
 int pick_tn(int M, int N) {
     int tn = 16;
     while (tn < M && tn < 256) tn *= 2;
     const long long wtiles = (N + kTileW - 1) / kTileW;
-    while (tn > 16 && 2 * wtiles * ((M + tn - 1) / tn) <= sm_count()) tn /= 2;
+    while (tn > 16 && 2 * wtiles * ((M + tn - 1) / tn) <= (long long)sm_count() * tc_ctas_per_sm(tn / 2)) tn /= 2;
     return tn;
 }
 

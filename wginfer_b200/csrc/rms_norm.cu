@@ -27,6 +27,10 @@ __global__ void __launch_bounds__(256) rms_warp_kernel(T *__restrict__ out, cons
     constexpr int V = Vec16<T>::N;
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    // launched with programmatic dependent launch: wait for the kernel that
+    // writes `in` before reading it (and before writing `out`)
+    pdl_trigger();
+    pdl_wait();
     if (row >= M) return;
     const int nvec = N / V;
     const T *x = in + (size_t)row * N;
@@ -186,11 +190,21 @@ int launch_rms(T *out, const T *in, const T *w, size_t M, size_t N, float eps, c
     const bool vec_ok = (N % V) == 0 && aligned16(out) && aligned16(in) && aligned16(w);
     const size_t nvec = N / V;
     if (vec_ok && nvec <= 32 * 8) {
-        int blocks = (int)((M + 7) / 8);
-        if (nvec <= 32 * 2) rms_warp_kernel<T, 2><<<blocks, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
-        else if (nvec <= 32 * 4) rms_warp_kernel<T, 4><<<blocks, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
-        else if (nvec <= 32 * 6) rms_warp_kernel<T, 6><<<blocks, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
-        else rms_warp_kernel<T, 8><<<blocks, 256, 0, s>>>(out, in, w, (int)M, (int)N, eps);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)((M + 7) / 8));
+        cfg.blockDim = dim3(256);
+        cfg.stream = s;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = pdl_enabled() ? 1 : 0;
+        cudaError_t e;
+        if (nvec <= 32 * 2) e = cudaLaunchKernelEx(&cfg, rms_warp_kernel<T, 2>, out, in, w, (int)M, (int)N, eps);
+        else if (nvec <= 32 * 4) e = cudaLaunchKernelEx(&cfg, rms_warp_kernel<T, 4>, out, in, w, (int)M, (int)N, eps);
+        else if (nvec <= 32 * 6) e = cudaLaunchKernelEx(&cfg, rms_warp_kernel<T, 6>, out, in, w, (int)M, (int)N, eps);
+        else e = cudaLaunchKernelEx(&cfg, rms_warp_kernel<T, 8>, out, in, w, (int)M, (int)N, eps);
+        if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "wgb_rms_norm: %s", cudaGetErrorString(e));
     } else if (vec_ok && nvec <= 256 * 8) {
         // up to 4 vectors of the row (and 4 of the weight) per thread: the
         // longest rows take 512 threads rather than 8 vectors a thread,
