@@ -375,8 +375,8 @@ def run_b200(args):
         "clocks": clk.summary(),
         # per step: embedding, 28 x (qkv gemv [rms, rope, kv append fused], attention,
         # o gemv [+residual], gate/up gemv [rms, swiglu fused], down gemv [+residual]), lm_head gemv
-        # [final rms fused], argmax, decode_end
-        "gpu_launches": K * (1 + 28 * 5 + 3),
+        # [final rms fused], argmax [+ sequence lengths advanced]
+        "gpu_launches": K * (1 + 28 * 5 + 2),
     })
     if not args.no_bs64:
         result["bs64"] = bs64(args, world, rank, local)

@@ -74,7 +74,7 @@ template <> __device__ __forceinline__ float vec_max<float>(const Vec16<float> &
 
 template <typename T, bool kVec, int kB>
 __global__ void __launch_bounds__(kThreads, kB > 8 ? 2 : 4) argmax_cluster_kernel(int64_t *max_idx, T *max_val, const T *vals,
-                                                                  size_t numel) {
+                                                                  size_t numel, int64_t *lens, int64_t maxlen) {
     constexpr int V = Vec16<T>::N;
     __shared__ unsigned long long red[kThreads / 32];
     cg::cluster_group cluster = cg::this_cluster();
@@ -160,12 +160,15 @@ __global__ void __launch_bounds__(kThreads, kB > 8 ? 2 : 4) argmax_cluster_kerne
             max_idx[row] = idx;
             if (max_val) max_val[row] = x[idx];
         }
+        // decode step: the row's sequence has grown by the token just chosen
+        if (lens && lens[row] < maxlen) lens[row] += 1;
     }
     cluster.sync();  // keep peers' shared memory alive until CTA 0 has read it
 }
 
 template <typename T>
-int launch_argmax(int64_t *idx, T *val, const T *vals, size_t rows, size_t numel, cudaStream_t s) {
+int launch_argmax(int64_t *idx, T *val, const T *vals, size_t rows, size_t numel, cudaStream_t s,
+                  int64_t *lens = nullptr, int64_t maxlen = 0) {
     constexpr int V = Vec16<T>::N;
     const bool vec = aligned16(vals) && (numel % V) == 0;
     // CTAs per row: up to kCluster, but no more than one wave of resident
@@ -205,14 +208,28 @@ int launch_argmax(int64_t *idx, T *val, const T *vals, size_t rows, size_t numel
     cfg.attrs = at;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
     cudaError_t e;
-    if (vec && few) e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true, kBFew>, idx, val, vals, numel);
-    else if (vec) e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true, kBWide>, idx, val, vals, numel);
-    else e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, false, kBWide>, idx, val, vals, numel);
+    if (vec && few)
+        e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true, kBFew>, idx, val, vals, numel, lens, maxlen);
+    else if (vec)
+        e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true, kBWide>, idx, val, vals, numel, lens, maxlen);
+    else e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, false, kBWide>, idx, val, vals, numel, lens, maxlen);
     if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "wgb_argmax: %s", cudaGetErrorString(e));
     return check_launch("wgb_argmax");
 }
 
 }  // namespace
+}  // namespace wgb
+
+namespace wgb {
+// Greedy step of batched decode: argmax of each logit row into tokens[row],
+// and lens[row] += 1 (up to maxlen) once the row's token is chosen, in one
+// launch.
+int argmax_rows_advance(int64_t *tokens, const void *logits, wginferDataType_t dtype, size_t rows, size_t numel,
+                        int64_t *lens, int64_t maxlen, cudaStream_t s) {
+    WGB_DISPATCH_FLOAT(dtype, T,
+        return launch_argmax(tokens, (T *)nullptr, (const T *)logits, rows, numel, s, lens, maxlen));
+    return WGB_OK;
+}
 }  // namespace wgb
 
 extern "C" int wgb_argmax_rows(int64_t *max_idx, void *max_val, const void *vals, wginferDataType_t dtype,

@@ -8,6 +8,11 @@
 
 namespace wgb {
 
+// Greedy step of batched decode (argmax.cu): tokens[r] = argmax of logits row
+// r, then lens[r] += 1 (up to maxlen), in one launch.
+int argmax_rows_advance(int64_t *tokens, const void *logits, wginferDataType_t dtype, size_t rows, size_t numel,
+                        int64_t *lens, int64_t maxlen, cudaStream_t s);
+
 // tcgen05 GEMM (linear_tc.cu): true when the tensor-core path takes this call.
 bool linear_tc_supported(size_t M, size_t N, size_t K, const void *out, const void *x, const void *w);
 int linear_tc_bf16(void *out, const void *x, const void *w, const void *bias, const void *residual, int M, int N,

@@ -110,11 +110,6 @@ __global__ void fill_positions_kernel(int64_t *pos, int64_t start, int n) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) pos[i] = start + i;
 }
 
-__global__ void decode_end_kernel(int64_t *lens, int B, int maxseq) {
-    const int b = blockIdx.x * blockDim.x + threadIdx.x;
-    if (b < B && lens[b] < maxseq) lens[b] += 1;
-}
-
 }  // namespace
 }  // namespace wgb
 
@@ -218,7 +213,7 @@ int attention(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t total_l
 
 // Positions of the layer's rows: the prefill chunk's (filled per chunk), or,
 // in batched decode, each sequence's current length (row b's new token sits
-// at lens[b]; decode_end advances lens after the step).
+// at lens[b]; the step's argmax advances lens once the token is chosen).
 const int64_t *positions(const wgbQwen2Model *M, int prefill_seq) { return prefill_seq >= 0 ? M->pos : M->lens; }
 
 // One transformer layer over T rows (model.cpp:243-328), REFERENCE numerics:
@@ -416,11 +411,10 @@ int decode_body(wgbQwen2Model *M, int B, bool ref) {
         if ((rc = run_layer(M, l, B, -1, 0, ref))) return rc;
     if ((rc = lm_head(M, M->x, B, M->logits, ref))) return rc;
     WGB_TRACE("lm_head_gemv+rms");
-    if ((rc = wgb_argmax_rows(M->tokens, nullptr, M->logits, M->dt, B, m.voc, s))) return rc;
-    WGB_TRACE("argmax");
-    decode_end_kernel<<<(B + 127) / 128, 128, 0, s>>>(M->lens, B, (int)m.maxseq);
-    WGB_TRACE("decode_end");
-    return cuda_err("decode_end");
+    // the greedy tokens, and every sequence one position longer
+    if ((rc = argmax_rows_advance(M->tokens, M->logits, M->dt, B, m.voc, M->lens, (int64_t)m.maxseq, s))) return rc;
+    WGB_TRACE("argmax+advance");
+    return WGB_OK;
 }
 
 int prefill_impl(wgbQwen2Model *M, int seq, const int64_t *ids_host, size_t n, bool ref) {
