@@ -27,7 +27,9 @@ namespace wgb {
 namespace {
 
 constexpr int kCluster = 8;
-constexpr int kThreads = 256;
+// threads per CTA: 512 (two CTAs per SM) when the rows fill the GPU, 256
+// for a few rows
+constexpr int kThreadsWide = 512, kThreadsFew = 256;
 // 16-byte vectors in flight per thread: 8 when the rows fill the GPU; 10 for
 // a few rows, where a 151936-wide bf16 row on 8 CTAs is then one round trip
 // (latency, not bandwidth, is what a few rows pay for)
@@ -72,8 +74,8 @@ template <> __device__ __forceinline__ float vec_max<float>(const Vec16<float> &
     return fmaxf(fmaxf(r.e[0], r.e[1]), fmaxf(r.e[2], r.e[3]));
 }
 
-template <typename T, bool kVec, int kB>
-__global__ void __launch_bounds__(kThreads, kB > 8 ? 2 : 4) argmax_cluster_kernel(int64_t *max_idx, T *max_val, const T *vals,
+template <typename T, bool kVec, int kB, int kThreads>
+__global__ void __launch_bounds__(kThreads, 2) argmax_cluster_kernel(int64_t *max_idx, T *max_val, const T *vals,
                                                                   size_t numel, int64_t *lens, int64_t maxlen) {
     constexpr int V = Vec16<T>::N;
     __shared__ unsigned long long red[kThreads / 32];
@@ -180,8 +182,10 @@ int launch_argmax(int64_t *idx, T *val, const T *vals, size_t rows, size_t numel
     int per_sm = dev >= 0 && dev < 64 ? resident[dev][vec ? 1 : 0].load(std::memory_order_relaxed) : 0;
     if (per_sm <= 0) {
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                &per_sm, vec ? argmax_cluster_kernel<T, true, kBWide> : argmax_cluster_kernel<T, false, kBWide>,
-                kThreads, 0) != cudaSuccess ||
+                &per_sm,
+                vec ? argmax_cluster_kernel<T, true, kBWide, kThreadsWide>
+                    : argmax_cluster_kernel<T, false, kBWide, kThreadsWide>,
+                kThreadsWide, 0) != cudaSuccess ||
             per_sm < 1) {
             cudaGetLastError();
             per_sm = 1;
@@ -196,7 +200,7 @@ int launch_argmax(int64_t *idx, T *val, const T *vals, size_t rows, size_t numel
     if (ns < 1) ns = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(rows * ns));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(vec && few ? kThreadsFew : kThreadsWide);
     cfg.stream = s;
     cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
@@ -209,10 +213,10 @@ int launch_argmax(int64_t *idx, T *val, const T *vals, size_t rows, size_t numel
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
     cudaError_t e;
     if (vec && few)
-        e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true, kBFew>, idx, val, vals, numel, lens, maxlen);
+        e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true, kBFew, kThreadsFew>, idx, val, vals, numel, lens, maxlen);
     else if (vec)
-        e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true, kBWide>, idx, val, vals, numel, lens, maxlen);
-    else e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, false, kBWide>, idx, val, vals, numel, lens, maxlen);
+        e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, true, kBWide, kThreadsWide>, idx, val, vals, numel, lens, maxlen);
+    else e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T, false, kBWide, kThreadsWide>, idx, val, vals, numel, lens, maxlen);
     if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "wgb_argmax: %s", cudaGetErrorString(e));
     return check_launch("wgb_argmax");
 }
