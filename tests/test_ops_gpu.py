@@ -131,12 +131,15 @@ def test_argmax_nan_semantics(oracle, cuda):
     assert idx.item() == 2 and val.item() == 3.0
 
 
+@pytest.mark.parametrize("reps", [1, 4])
+@pytest.mark.parametrize("n", [4096, 4093])
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16, torch.float32])
-def test_argmax_rows_special_values(oracle, cuda, dt):
-    """Vectorised rows with NaNs, signed-zero maxima, -inf rows, all-NaN rows
-    and ties inside one 16-byte vector, against the oracle's sequential scan
-    (argmax_cpu.cpp:26-47)."""
-    n = 4096
+def test_argmax_rows_special_values(oracle, cuda, dt, n, reps):
+    """Rows with NaNs, signed-zero maxima, -inf rows, all-NaN rows and ties
+    inside one 16-byte vector, against the oracle's sequential scan
+    (argmax_cpu.cpp:26-47). 7 rows take the few-rows launch (8-CTA clusters
+    of 256 threads), 28 rows the many-rows one (512-thread CTAs); a width
+    of 4093 takes the element-wise path (rows not 16-byte aligned)."""
     g = torch.Generator("cpu").manual_seed(3)
     rows = []
     r = -torch.rand(n, generator=g) - 1.0; r[100] = 0.0; r[50] = -0.0; rows.append(r)  # -0 first, then +0
@@ -145,14 +148,14 @@ def test_argmax_rows_special_values(oracle, cuda, dt):
     r = torch.full((n,), float("nan")); r[4000] = -5.0; rows.append(r)  # the only number
     r = torch.full((n,), float("nan")); rows.append(r)  # all NaN: index 0
     r = torch.randn(n, generator=g); r[0] = float("nan"); rows.append(r)  # NaN at index 0 wins
-    r = torch.randn(n, generator=g); r[17] = float("inf"); r[4095] = float("inf"); rows.append(r)
-    vals = torch.stack(rows).to(dt).cuda()
-    idx = torch.empty(len(rows), dtype=torch.int64, device="cuda")
-    val = torch.empty(len(rows), dtype=dt, device="cuda")
+    r = torch.randn(n, generator=g); r[17] = float("inf"); r[n - 1] = float("inf"); rows.append(r)
+    vals = torch.stack(rows * reps).to(dt).cuda()
+    idx = torch.empty(vals.shape[0], dtype=torch.int64, device="cuda")
+    val = torch.empty(vals.shape[0], dtype=dt, device="cuda")
     ops.argmax_rows(idx, val, vals)
     code = {torch.bfloat16: 15, torch.float16: 12, torch.float32: 13}[dt]
     host = vals.cpu()
-    for i in range(len(rows)):
+    for i in range(vals.shape[0]):
         row = host[i].numpy() if dt == torch.float32 else host[i].view(torch.int16).numpy().view(np.uint16)
         want_i, _ = oracle.argmax(np.ascontiguousarray(row), code)
         assert idx[i].item() == want_i, (i, idx[i].item(), want_i)
