@@ -13,13 +13,20 @@ needed between steps.
 (wgb_qwen2_infer: host token in, host token out), with the 8-byte
 host->device and device->host copies inside the timed region.
 
-Extra objects: `bs64` (64 sequences with 2048-token prompts on the
-one-layer model, requests split across the GPUs), `roofline` (the weight-
-streaming GEMV, the dominant kernel), `cpu_baseline` (the reference's own CPU
-build timed on a bounded sample), `clocks`.
+`value` is measured in FAST numerics (the default mode: f32 sums in the
+fastest order). `reference_numerics` is the same measurement in REFERENCE
+numerics, the mode whose greedy tokens are identical to the reference's
+(every sum in the reference CPU backend's order; tests/test_model_gpu.py
+checks the streams), on the same model in the same run.
+
+Extra objects: `roofline` (the weight-streaming GEMV, the dominant kernel),
+`cpu_baseline` (the reference's own CPU build timed on a bounded sample),
+`clocks`, `op_bandwidth`, and at the end of the line `bs64` (64 sequences
+with 2048-token prompts on the one-layer model, requests split across the
+GPUs: a strong-scaling workload) and `reference_numerics`.
 
 `--impl reference` times the reference's own CPU implementation
-(oracle/_ref) on the host cores for the same metric.
+(oracle/_ref, the full 28-layer Model) on the host cores for the same metric.
 """
 from __future__ import annotations
 
@@ -316,11 +323,51 @@ def op_sweep(peak, quick=False):
 
 
 def decode_config(args, world):
-    """The workload both arms report (the metric is quoted on it)."""
+    """The workload the B200 arm reports (the metric is quoted on it)."""
     return {"workload": "Qwen2-1.5B arch (28 layers, hidden 1536, 12/2 heads x 128, MLP 8960, vocab "
                         "151936), greedy decode, batch 1 per GPU, prompt %d" % args.prompt,
             "global_batch": world, "seq_len": args.prompt + args.steps, "parallelism": f"replicas x{world}",
             "numerics": args.numerics, "l2": "weights 3.1 GB > L2; no flush needed"}
+
+
+def time_e2e(m, K, W, world):
+    """K decode steps through Qwen2.infer (wgb_qwen2_infer: the token copied
+    host->device and the next token device->host every step), device-timed."""
+    import torch
+    s = m.torch_stream()
+    tok = m.tokens(1)[0]
+    for _ in range(W):
+        tok = m.infer([tok])
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(K):
+        tok = m.infer([tok])
+    e1.record(s)
+    e1.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
+
+
+def reference_numerics_leg(m, args, world, rank, bytes_per_token, peak):
+    """The same decode in REFERENCE numerics (token-identical to the
+    reference) on the same model: fresh cache, the same prompt, K graph
+    steps device-timed, then K steps end to end."""
+    from wginfer_b200 import numerics
+    from wginfer_b200.synthetic import prompt_ids
+    K, W = args.steps, args.warmup
+    with numerics("reference"):
+        m.reset_cache()
+        m.prefill(0, prompt_ids(args.prompt, m.cfg.voc, seed=rank).numpy())
+        t = max_over_ranks(time_decode(m, 1, K, W, world), world)
+        te = time_e2e(m, K, W, world)
+    value = world * K / t
+    return {"value": round(value, 2), "unit": UNIT, "ms_per_step": round(t / K * 1e3, 4),
+            "weight_stream_roofline_frac": round(value / world / (peak * 1e9 / bytes_per_token), 4),
+            "e2e": {"value": round(world * K / te, 2), "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
+            "greedy_tokens": "identical to the reference CPU backend's (REFERENCE numerics)",
+            "gpu_launches": K * (1 + 28 * 5 + 1)}
 
 
 def run_b200(args):
@@ -344,26 +391,16 @@ def run_b200(args):
         t_max = max_over_ranks(t, world)
         value = world * K / t_max
         # e2e through the public API: host token in, host token out, every step
-        s = m.torch_stream()
-        tok = m.tokens(1)[0]
-        for _ in range(W):
-            tok = m.infer([tok])
-        torch.cuda.synchronize()
-        barrier(world)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(s)
-        for _ in range(K):
-            tok = m.infer([tok])
-        e1.record(s)
-        e1.synchronize()
-        barrier(world)
-        te = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
+        te = time_e2e(m, K, W, world)
         roof = gemv_roofline(kept["out_embed"], cfg, peak)
         roof["peak_source"] = peak_src
         del kept
-        m.close()
-        torch.cuda.empty_cache()
     bytes_per_token = cfg.weight_bytes()
+    ref_leg = None
+    if args.numerics == "fast" and not args.no_reference_numerics:
+        ref_leg = reference_numerics_leg(m, args, world, rank, bytes_per_token, peak)
+    m.close()
+    torch.cuda.empty_cache()
     result.update({
         "value": round(value, 2), "ms_per_step": round(t_max / K * 1e3, 4),
         "config": decode_config(args, world),
@@ -378,12 +415,16 @@ def run_b200(args):
         # [final rms fused], argmax [+ sequence lengths advanced]
         "gpu_launches": K * (1 + 28 * 5 + 2),
     })
-    if not args.no_bs64:
-        result["bs64"] = bs64(args, world, rank, local)
+    # the long sweep first; the batched and REFERENCE results close the line
+    # (a reader of its last characters sees them)
     if rank == 0 and not args.no_sweep:
         result["op_bandwidth"] = op_sweep(peak, quick=world > 1)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        result["cpu_baseline"] = cpu_baseline(args.cpu_steps)
+    if not args.no_bs64:
+        result["bs64"] = bs64(args, world, rank, local)
+    if ref_leg is not None:
+        result["reference_numerics"] = ref_leg
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -412,60 +453,68 @@ def bs64(args, world, rank, local):
         t = time_decode(m, per, K, W, world)
         m.close()
     t_max = max_over_ranks(t, world)
+    # HBM bytes one GPU's step must move: every weight once (the layer, the
+    # final norm, lm_head) and its sequences' K/V (2 x 2 heads x 128 x 2 B
+    # per cached position) at the mean cache length of the timed steps
+    peak, _ = load_peaks()
+    cache = 2048 + W + K / 2
+    step_bytes = cfg.weight_bytes() + per * cache * 2 * cfg.nkvh * cfg.dh * 2
     return {"value": round(total * K / t_max, 1), "unit": UNIT, "sequences": total, "per_gpu": per,
             "prompt": 2048, "steps": K, "ms_per_step": round(t_max / K * 1e3, 4), "scaling": "strong",
-            "prefill_s_rank0": round(prefill_s, 2),
-            "workload": "one-layer Qwen2 (config-2 layer + embeddings + lm_head), bf16, greedy"}
+            "hbm_frac": round(step_bytes / (t_max / K) / 1e9 / peak, 3), "prefill_s_rank0": round(prefill_s, 2),
+            "workload": "one-layer Qwen2 (the config-2 layer + embeddings + lm_head), bf16, greedy"}
 
 
 # ---------------------------------------------------------------- reference CPU arm
-def reference_decode_sample(budget_s: float, steps: int | None = None, warmup: int = 1):
-    """The reference's Model::infer (oracle/_ref) on the host cores, one
-    decode token per step on 1- and 2-layer models of the full dimensions;
-    the full 28-layer token time is extrapolated as t1 + 27 (t2 - t1)."""
-    import numpy as np
+def reference_model():
+    """The reference's own Model (oracle/_ref, its CPU device) with the
+    28-layer Qwen2-1.5B architecture and the same seeded weights the tests
+    use (~3 GB of bf16 on the host)."""
     from oracle import oracle as O
     from tests.golden import cases as CS
     from wginfer_b200.synthetic import Qwen2Config
-    ref = O.Reference()
-    models = []
-    for nl in (1, 2):
-        cfg = Qwen2Config(nlayer=nl, maxseq=64)
-        meta, w = CS.model_inputs(cfg, seed=0)
-        m = O.ReferenceQwen2(ref, meta, w)
-        m.infer(np.array([1], np.int64))
-        models.append((m, w))
-    per_token = []
-    t_start = time.time()
-    n = 0
-    while True:
-        t1s = time.perf_counter()
-        models[0][0].infer(np.array([2], np.int64))
-        t1 = time.perf_counter() - t1s
-        t2s = time.perf_counter()
-        models[1][0].infer(np.array([2], np.int64))
-        t2 = time.perf_counter() - t2s
-        n += 1
-        if n > warmup:
-            per_token.append(t1 + 27 * max(t2 - t1, 0.0))
-        if steps is not None and n >= steps + warmup:
-            break
-        if steps is None and time.time() - t_start > budget_s and per_token:
-            break
-    return per_token
+    cfg = Qwen2Config(nlayer=28, maxseq=256)
+    meta, w = CS.model_inputs(cfg, seed=0)
+    m = O.ReferenceQwen2(O.Reference(), meta, w)
+    del w
+    return m
 
 
-def cpu_baseline(budget_s):
+def reference_decode_times(steps: int, warmup: int):
+    """Seconds per decode token of the reference Model::infer, batch 1, for
+    `steps` tokens after `warmup` untimed ones. The prompt is one token, so
+    the cache holds 1..steps+warmup+1 positions (a longer prompt would need a
+    prefill that forms logits for every prompt row, minutes on the CPU;
+    attention over 512 positions is under 1% of the CPU token time, which is
+    the linears')."""
+    import numpy as np
+    m = reference_model()
+    tok = m.infer(np.array([1], np.int64))
+    for _ in range(warmup):
+        tok = m.infer(np.array([tok], np.int64))
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        tok = m.infer(np.array([tok], np.int64))
+        times.append(time.perf_counter() - t0)
+    del m
+    return times
+
+
+REF_SAMPLE = ("decode tokens of the reference Model::infer (oracle/_ref, the full 28-layer Qwen2-1.5B "
+              "architecture on its CPU device, batch 1, greedy), prompt 1 token, cache 1..%d positions; "
+              "its linear is single-threaded below 64 rows")
+
+
+def cpu_baseline(steps: int):
     try:
         from oracle import oracle as O
         if not os.path.exists(O.REF_SO):
             return {"value": None, "unavailable": "oracle/_ref not built"}
-        per = reference_decode_sample(budget_s, warmup=0)
-        v = 1.0 / statistics.median(per)
+        per = reference_decode_times(steps, warmup=1)
+        v = len(per) / sum(per)
         return {"value": round(v, 4), "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
-                "sample": f"{len(per)} decode tokens of the reference Model on 1- and 2-layer models of the "
-                          "full dimensions (batch 1; its linear is single-threaded below 64 rows), 28-layer "
-                          "time extrapolated as t1 + 27 (t2 - t1)"}
+                "sample": f"{len(per)} " + REF_SAMPLE % (len(per) + 2)}
     except Exception as e:  # reported, never fatal for the GPU arm
         return {"value": None, "unavailable": f"{type(e).__name__}: {e}"}
 
@@ -479,21 +528,21 @@ def run_reference(args):
     if not os.path.exists(O.REF_SO):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (reference CPU build) missing"}))
         return
-    # bound the whole run to a few minutes: cap the number of sampled tokens
-    steps = max(1, min(args.steps, args.ref_max_steps))
-    per = reference_decode_sample(0, steps=steps, warmup=min(args.warmup, 1))
+    K, W = args.steps, args.warmup
+    per = reference_decode_times(K, W)
     t = sum(per)
-    value = len(per) / t
+    value = K / t
     cores = os.cpu_count()
+    config = {"workload": "Qwen2-1.5B arch (28 layers, hidden 1536, 12/2 heads x 128, MLP 8960, vocab 151936), "
+                          "greedy decode, batch 1, reference CPU Model, prompt 1 token",
+              "global_batch": 1, "seq_len": 1 + W + K + 1, "parallelism": "one host process (rank 0)",
+              "numerics": "the reference's own", "l2": "n/a (CPU)"}
     out = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
-           "steps": len(per), "warmup": min(args.warmup, 1), "ms_per_step": round(t / len(per) * 1e3, 2),
+           "steps": K, "warmup": W, "ms_per_step": round(t / K * 1e3, 2),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-           "data": "synthetic (seeded random weights)",
-           "config": decode_config(args, world),
+           "data": "synthetic (seeded random weights)", "config": config,
            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "reference",
-                            "sample": "per step one decode token of the reference Model::infer (oracle/_ref, "
-                                      "its CPU device) on 1- and 2-layer models of the full dimensions at a short "
-                                      "cache; 28-layer time = t1 + 27 (t2 - t1)"},
+                            "sample": f"{K} " + REF_SAMPLE % (W + K + 1)},
            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
@@ -510,9 +559,11 @@ def main():
     ap.add_argument("--only-bs64", action="store_true",
                     help="print only the batched-decode result (64 sequences x 2048-token prompts)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-numerics", action="store_true",
+                    help="skip the REFERENCE-numerics (token-identical) decode measurement")
     ap.add_argument("--no-sweep", action="store_true", help="skip the elementwise/reduction bandwidth sweep")
-    ap.add_argument("--cpu-seconds", type=float, default=20.0)
-    ap.add_argument("--ref-max-steps", type=int, default=12)
+    ap.add_argument("--cpu-steps", type=int, default=2,
+                    help="decode tokens of the reference CPU Model timed for cpu_baseline (~6 s each)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -159,13 +159,16 @@ __export int wgb_self_attention_ex(void *attn_val, const void *q, const void *k,
  * driver. No counterpart in the reference. Its scratch is one file-scope
  * device array of wgb_self_attention_noalloc_max_scratch() bytes (4 MiB),
  * held by every GPU that loads the library until exit; sizes whose scratch
- * would exceed it return WGB_ERR_OUT_OF_RANGE. The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress), so make that
- * first call before any stream capture. Calls allocate nothing. All calls on
- * a device share the array, which keeps the last call's contents; nothing in
- * it has to start at zero (every scratch word a call reads is written earlier
- * in that call), but calls whose kernels overlap on the same device, e.g. on
- * two streams, race: serialise them, e.g. on one stream. */
+ * would exceed it return WGB_ERR_OUT_OF_RANGE. Every call looks up the
+ * array's device address (cudaGetSymbolAddress) with the caller's device
+ * current; the first call on a device also loads the library's device code
+ * there, so make that first call before any stream capture. Calls allocate
+ * nothing. The scratch holds REFERENCE numerics' one score per key for caches
+ * longer than shared memory holds. All calls on a device share the array,
+ * which keeps the last call's contents; nothing in it has to start at zero
+ * (every score a call reads is written earlier in that call), but calls whose
+ * kernels overlap on the same device, e.g. on two streams, race: serialise
+ * them, e.g. on one stream. */
 __export int wgb_self_attention_noalloc(void *attn_val, const void *q, const void *k, const void *v,
                                         wginferDataType_t dtype, size_t seqlen, size_t nhead,
                                         size_t nkvhead, size_t d, size_t dv, size_t total_len,
@@ -210,8 +213,9 @@ __export int wgb_qwen2_reset_cache(wgbQwen2Model *model);
 /* Model::infer for sequence 0 (model.cpp:371-415): token_ids are host
  * memory; runs them through the model (prefill when ntoken > 1), appends to
  * the KV cache and returns the next token in *next (host). Greedy when
- * top_k == 1, top_p >= 1 and temperature == 1, else samples on the host from
- * the last row's logits like the reference. Synchronises the model stream. */
+ * top_k == 1, top_p >= 1 and temperature == 1, else samples from the last
+ * row's logits on the device with the reference's rules (wgb_sample_rows);
+ * only the drawn token is copied back. Synchronises the model stream. */
 __export int wgb_qwen2_infer(wgbQwen2Model *model, const int64_t *token_ids, size_t ntoken,
                              int top_k, float top_p, float temperature, int64_t *next);
 

@@ -26,11 +26,13 @@ _NP = {DT_F32: np.float32, DT_BF16: np.uint16, DT_F16: np.uint16}
 
 
 def build(reference_root: str | None = None, quiet: bool = True) -> None:
-    """Build liboracle.so, and the reference library when its sources exist."""
+    """Build liboracle.so, and the reference library when its source tree is
+    given (the argument, else the WGINFER_REF_ROOT environment variable) and
+    exists."""
     out = subprocess.DEVNULL if quiet else None
     subprocess.check_call(["make", "-C", HERE, "oracle"], stdout=out)
-    ref = reference_root or "/root/reference"
-    if os.path.isdir(os.path.join(ref, "src")):
+    ref = reference_root or os.environ.get("WGINFER_REF_ROOT")
+    if ref and os.path.isdir(os.path.join(ref, "src")):
         subprocess.check_call(["make", "-C", HERE, "ref", f"REF={ref}"], stdout=out)
 
 

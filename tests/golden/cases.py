@@ -162,6 +162,7 @@ def run_case(lib, case, ins=None):
 # ---- Qwen2 token streams -------------------------------------------------
 TINY = Qwen2Config(nlayer=2, hs=256, nh=4, nkvh=2, dh=64, di=512, voc=1000, maxseq=256)
 ONE_LAYER = Qwen2Config(nlayer=1, maxseq=640)          # the config-2 layer with embeddings and lm_head
+ONE_LAYER_2K = Qwen2Config(nlayer=1, maxseq=2048 + 256)  # the same model with room for 2048-token prompts
 FULL = Qwen2Config(nlayer=28, maxseq=640)              # Qwen2-1.5B architecture
 
 # name -> (config, prompt length, generated tokens)
@@ -169,7 +170,22 @@ SMALL_MODELS = {
     "tiny_p16_g64": (TINY, 16, 64),
     "tiny_p100_g32": (TINY, 100, 32),
     "one_layer_p16_g12": (ONE_LAYER, 16, 12),
+    # one decoder layer, 512-token prefill, 128 decode steps
+    "one_layer_p512_g128": (ONE_LAYER, 512, 128),
 }
+
+# Batched decode: 64 sequences with uniform random 2048-token prompts (ids
+# from prompt_ids(2048, voc, seed=prompt_seed, batch=64)) decoded together on
+# the one-layer model; the streams of the `checked` sequences are stored.
+BATCHED = {
+    "one_layer_bs64_p2048": dict(cfg=ONE_LAYER_2K, prompt=2048, sequences=64, prompt_seed=1000,
+                                 checked=[0, 21, 42, 63], steps=16),
+}
+
+
+def batched_prompts(spec) -> np.ndarray:
+    from wginfer_b200.synthetic import prompt_ids
+    return prompt_ids(spec["prompt"], spec["cfg"].voc, seed=spec["prompt_seed"], batch=spec["sequences"]).numpy()
 # name -> (config, prompt length, generated tokens, tokens checked against the reference itself)
 FULL_MODELS = {
     "qwen2_1p5b_p16_g128": (FULL, 16, 128, 3),

@@ -5,12 +5,17 @@ Run from the repo root, in a container where the reference tree exists
 
     python tests/golden/make_golden.py            # ops + small models
     python tests/golden/make_golden.py --full     # + 28-layer token streams
+    python tests/golden/make_golden.py --skip-ops --only NAME ...   # selected streams
 
 Inputs are regenerated from seeds by tests/golden/cases.py, so only outputs
 are stored: bits for small outputs, SHA-256 of the bits for large ones.
 Op outputs come from the reference build (oracle/_ref); the 28-layer Qwen2
 streams come from the oracle restatement (the reference takes ~18 s per token
-there) after its first tokens were checked against the reference itself.
+there) after its first tokens were checked against the reference itself. The
+batched streams (64 sequences with 2048-token prompts on the one-layer model)
+come from the oracle, decoding each checked sequence on its own (sequences in
+a batch are independent); the reference would take about 15 minutes per
+2048-token prefill because it forms logits for every prompt row.
 """
 from __future__ import annotations
 
@@ -79,10 +84,38 @@ def model_stream(model_cls, lib, cfg, prompt_len, steps, seed=0, logits=False):
     return toks, margins
 
 
-def models_golden(ref, ora, full: bool) -> None:
+def batched_golden(ora, name, spec):
+    meta, w = CS.model_inputs(spec["cfg"], 0)
+    ids = CS.batched_prompts(spec)
+    streams, margins = {}, {}
+    for seq in spec["checked"]:
+        m = O.OracleQwen2(ora, meta, w)
+        t, lg = m.infer(ids[seq], want_logits=True)
+        toks, mg = [t], [CS.top2_margin(lg)]
+        for _ in range(spec["steps"] - 1):
+            t, lg = m.infer(np.array([t]), want_logits=True)
+            toks.append(t)
+            mg.append(CS.top2_margin(lg))
+        streams[str(seq)], margins[str(seq)] = toks, mg
+        del m
+    return {"streams": streams, "margins": margins,
+            "source": "oracle, each checked sequence decoded on its own"}
+
+
+def models_golden(ref, ora, full: bool, only=None) -> None:
     path = os.path.join(HERE, "qwen2_streams.json")
     out = json.load(open(path)) if os.path.exists(path) else {}
+    for name, spec in CS.BATCHED.items():
+        if only is not None and name not in only:
+            continue
+        t0 = time.time()
+        out[name] = batched_golden(ora, name, spec)
+        print(f"{name}: {len(spec['checked'])} streams in {time.time() - t0:.1f}s", flush=True)
+        with open(path, "w") as f:
+            json.dump(out, f, indent=1)
     for name, (cfg, plen, steps) in CS.SMALL_MODELS.items():
+        if only is not None and name not in only:
+            continue
         t0 = time.time()
         rt, _ = model_stream(O.ReferenceQwen2, ref, cfg, plen, steps)
         ot, om = model_stream(O.OracleQwen2, ora, cfg, plen, steps, logits=True)
@@ -91,6 +124,8 @@ def models_golden(ref, ora, full: bool) -> None:
         print(f"{name}: {len(rt)} tokens in {time.time() - t0:.1f}s", flush=True)
     if full:
         for name, (cfg, plen, steps, ref_prefix) in CS.FULL_MODELS.items():
+            if only is not None and name not in only:
+                continue
             t0 = time.time()
             ot, om = model_stream(O.OracleQwen2, ora, cfg, plen, steps, logits=True)
             rt, _ = model_stream(O.ReferenceQwen2, ref, cfg, plen, ref_prefix) if ref_prefix else ([], [])
@@ -108,9 +143,11 @@ if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--full", action="store_true")
     ap.add_argument("--skip-ops", action="store_true")
+    ap.add_argument("--only", nargs="*", default=None, help="stream names to (re)generate")
+    ap.add_argument("--reference-root", default=None, help="reference source tree (for oracle/_ref)")
     a = ap.parse_args()
-    O.build()
+    O.build(a.reference_root)
     ref, ora = O.Reference(), O.Oracle()
     if not a.skip_ops:
         ops_golden(ref)
-    models_golden(ref, ora, a.full)
+    models_golden(ref, ora, a.full or bool(a.only), a.only)

@@ -38,7 +38,7 @@ def run_stream(m, plen, steps, seed=0):
     return m.generate(CS.prompt(plen, m.cfg.voc, seed), steps, stop_at_eos=False)
 
 
-@pytest.mark.parametrize("name", ["tiny_p16_g64", "tiny_p100_g32", "one_layer_p16_g12"])
+@pytest.mark.parametrize("name", ["tiny_p16_g64", "tiny_p100_g32", "one_layer_p16_g12", "one_layer_p512_g128"])
 def test_stream_reference_numerics(cuda, name):
     cfg, plen, steps = CS.SMALL_MODELS[name]
     with numerics("reference"):
@@ -46,15 +46,7 @@ def test_stream_reference_numerics(cuda, name):
     assert toks == STREAMS[name]["tokens"]
 
 
-# With a 512-token prompt the stream first differs at step 76. The oracle
-# reproduces that divergence exactly when its expf is replaced by the
-# correctly rounded exp the device evaluates, so the cause is glibc's expf,
-# which is not correctly rounded (it differs on ~8e-5 of inputs).
-P512_XFAIL = pytest.mark.xfail(reason="glibc expf is not correctly rounded; device exp is", strict=False)
-
-
-@pytest.mark.parametrize("name", ["qwen2_1p5b_p16_g128", "qwen2_1p5b_p128_g128",
-                                  pytest.param("qwen2_1p5b_p512_g128", marks=P512_XFAIL)])
+@pytest.mark.parametrize("name", ["qwen2_1p5b_p16_g128", "qwen2_1p5b_p128_g128", "qwen2_1p5b_p512_g128"])
 def test_full_model_stream_reference_numerics(cuda, name):
     if name not in STREAMS:
         pytest.skip(f"golden stream {name} not generated")
@@ -66,8 +58,8 @@ def test_full_model_stream_reference_numerics(cuda, name):
     assert toks == gold, f"first divergence at step {first}"
 
 
-@pytest.mark.parametrize("name", ["tiny_p16_g64", "tiny_p100_g32", "one_layer_p16_g12", "qwen2_1p5b_p16_g128",
-                                  "qwen2_1p5b_p512_g128"])
+@pytest.mark.parametrize("name", ["tiny_p16_g64", "tiny_p100_g32", "one_layer_p16_g12", "one_layer_p512_g128",
+                                  "qwen2_1p5b_p16_g128", "qwen2_1p5b_p512_g128"])
 def test_stream_fast_numerics_teacher_forced(cuda, name):
     """(The 512-token prompt runs its projections on the tensor cores with
     256-row input tiles and K split across CTAs.)"""
@@ -87,6 +79,31 @@ def test_stream_fast_numerics_teacher_forced(cuda, name):
             assert a == b, f"step {i}: margin {mg} but tokens differ"
     agree = sum(a == b for a, b in zip(got, gold)) / len(gold)
     print(f"{name}: FAST teacher-forced agreement {agree:.3f}")
+
+
+def test_batched_64_sequences_2048_prompts_reference_numerics(cuda):
+    """64 sequences with 2048-token prompts decoded together on the one-layer
+    model, in REFERENCE numerics, through the batch-64 decode graph: the
+    streams of the checked sequences equal the oracle's, which decoded each
+    of them on its own (model.cpp:371-415)."""
+    spec = CS.BATCHED["one_layer_bs64_p2048"]
+    gold = STREAMS["one_layer_bs64_p2048"]["streams"]
+    B, steps = spec["sequences"], spec["steps"]
+    ids = CS.batched_prompts(spec)
+    with numerics("reference"):
+        m = model(spec["cfg"], max_batch=B)
+        m.reset_cache()
+        for b in range(B):
+            m.prefill(b, ids[b])
+        seqs = [[t] for t in m.tokens(B)]
+        for _ in range(steps - 1):
+            m.decode_step(B)
+            for b, t in enumerate(m.tokens(B)):
+                seqs[b].append(t)
+    for seq, want in gold.items():
+        got = seqs[int(seq)]
+        first = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), None)
+        assert got == want, f"sequence {seq}: first divergence at step {first}"
 
 
 @pytest.mark.parametrize("mode", ["fast", "reference"])
@@ -187,3 +204,45 @@ def test_checkpoint_load_matches_direct_weights(cuda, tmp_path):
         got = m.generate(ids, 12, stop_at_eos=False)
         del m
     assert got == want
+
+
+def _bf16_bits_of_f32(a):
+    return (np.ascontiguousarray(a, np.float32).view(np.uint32) >> 16).astype(np.uint16)
+
+
+@pytest.mark.parametrize("mode", ["fast", "reference"])
+@pytest.mark.parametrize("B", [1, 3])
+def test_decode_step_fused_argmax_ties_and_nan(oracle, cuda, mode, B):
+    """The decode step's greedy token comes out of the lm_head launch itself
+    (a (value, first index) key folded across CTAs, model.cpp:398-407 /
+    argmax_cpu.cpp:26-47). Each step's tokens must equal the oracle's
+    sequential argmax of the logits that same launch wrote: with lm_head rows
+    repeating every 7 rows (every maximum is tied 143 times), with NaN logits
+    at index 0 (the scan keeps them) and elsewhere (never chosen)."""
+    cfg = CS.TINY
+    w = qwen2_weights(cfg, seed=0)
+    base = w["out_embed"].clone()
+    prompts = [CS.prompt(6 + 5 * b, cfg.voc, seed=b + 40) for b in range(B)]
+    variants = {"plain": base.clone(), "periodic": base[torch.arange(cfg.voc) % 7].clone()}
+    nan0 = base.clone()
+    nan0[0] = float("nan")
+    variants["nan_at_0"] = nan0
+    nan5 = base[torch.arange(cfg.voc) % 7].clone()
+    nan5[5] = float("nan")
+    variants["nan_at_5_periodic"] = nan5
+    with numerics(mode):
+        m = model(cfg, max_batch=B)
+        for name, emb in variants.items():
+            m.set_weight("out_embed", emb)
+            m.reset_cache()
+            for b, p in enumerate(prompts):
+                m.prefill(b, p)
+            for step in range(3):
+                m.decode_step(B)
+                toks = m.tokens(B)
+                for b in range(B):
+                    want, _ = oracle.argmax(_bf16_bits_of_f32(m.logits(b)), 15)
+                    assert toks[b] == want, (name, step, b, toks[b], want)
+            if name == "nan_at_0":
+                assert toks == [0] * B
+    m.set_weight("out_embed", base)

@@ -14,14 +14,14 @@ from wginfer_b200 import numerics, ops
 pytestmark = pytest.mark.gpu
 
 EXACT_OPS = {"add", "embedding", "argmax"}
-# f32 outputs of ops that evaluate exp/sin/cos: REFERENCE numerics round those
-# functions correctly (double evaluation), while glibc's f32 versions are off
-# by one ulp on some inputs (measured: expf on 7.6e-5 of all floats, sinf/cosf
-# on 1.3% of RoPE angles). The output then differs by about one ulp of the
-# terms it is formed from (RoPE's a*cos - b*sin can cancel, so this is an
-# absolute bound, not a relative one). bf16 outputs absorb these differences
-# and stay bit-identical.
-TRANSCENDENTAL_ATOL = {"rope": 1e-6, "swiglu": 1e-6, "self_attention": 1e-6}
+# f32 RoPE evaluates sin/cos/pow: REFERENCE numerics round those correctly
+# (double evaluation), while glibc's f32 sinf/cosf are off by one ulp on about
+# 1.3% of RoPE angles. The output then differs by about one ulp of the terms it
+# is formed from (a*cos - b*sin can cancel, so this is an absolute bound, not a
+# relative one). bf16 outputs absorb these differences and stay bit-identical.
+# exp (swiglu, the attention softmax) is the C library's expf restated
+# (libm_expf.cuh), so those ops are bit-identical at f32 too.
+TRANSCENDENTAL_ATOL = {"rope": 1e-6}
 
 
 def as_f32(a):
@@ -300,10 +300,11 @@ def test_attention_prefill_vs_torch(cuda, S, L, nh, nkvh, d, dt):
     torch.testing.assert_close(out.float(), _attn_ref(q, k, v, scale), rtol=2e-2, atol=1e-2)
 
 
-def test_attention_workspace_contract(cuda):
+def test_attention_workspace_contract(oracle, cuda):
     """FAST needs no workspace (the cluster folds its key slices in shared
     memory); REFERENCE keeps one score per key in the workspace once the cache
-    is longer than shared memory holds."""
+    is longer than shared memory holds. Both REFERENCE entry points are
+    bit-identical to the oracle there."""
     import ctypes as C
     from wginfer_b200 import _lib
     l = _lib.lib()
@@ -327,13 +328,18 @@ def test_attention_workspace_contract(cuda):
         out2 = torch.empty_like(q)
         ops.self_attention(out2, q, k, v, 0.088)
     torch.cuda.synchronize()
-    assert torch.equal(out, out2)
+    h = lambda t: t.cpu().view(torch.int16).numpy().view(np.uint16)
+    want = np.zeros((1, 12, 128), np.uint16)
+    oracle.self_attention(want, h(q), h(k), h(v), 0.088, 15)
+    assert np.array_equal(h(out), want)
+    assert np.array_equal(h(out2), want)
 
 
 @pytest.mark.parametrize("mode", ["fast", "reference"])
-@pytest.mark.parametrize("L", [1, 63, 64, 65, 700, 2304])
+@pytest.mark.parametrize("L", [1, 63, 64, 65, 700, 2304, 12000, 16000])
 def test_attention_decode_lengths(oracle, cuda, mode, L):
-    """Single-query decode over cache lengths around the tile size."""
+    """Single-query decode over cache lengths around the tile size; past
+    11000 keys REFERENCE keeps its scores in the global workspace."""
     q, k, v = _bf16((1, 12, 128), L), _bf16((L, 2, 128), L + 1), _bf16((L, 2, 128), L + 2)
     out = torch.empty_like(q)
     with numerics(mode):
@@ -345,3 +351,23 @@ def test_attention_decode_lengths(oracle, cuda, mode, L):
         assert np.array_equal(h(out), want)
     else:
         np.testing.assert_allclose(as_f32(h(out)), as_f32(want), rtol=2e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("up", [1.0, -3.5])
+def test_swiglu_f32_reference_exp_sweep(oracle, cuda, up):
+    """REFERENCE swiglu at f32 over every 61st 32-bit pattern of the gate
+    (70 M values: normals, subnormals, both overflow edges, inf and NaN),
+    bit-identical to the oracle, whose exp is the host C library's expf."""
+    bits = np.arange(0, 1 << 32, 61, dtype=np.uint64).astype(np.uint32)
+    gate = bits.view(np.float32)
+    upv = np.full_like(gate, up)
+    want = np.zeros_like(gate)
+    oracle.swiglu(want, gate, upv, 13)
+    g = torch.from_numpy(gate).cuda()
+    out = torch.empty_like(g)
+    with numerics("reference"):
+        ops.swiglu(out.view(1, -1), g.view(1, -1), torch.from_numpy(upv).cuda().view(1, -1))
+    got = out.cpu().numpy()
+    same = (got.view(np.uint32) == want.view(np.uint32)) | (np.isnan(got) & np.isnan(want))
+    bad = np.flatnonzero(~same)
+    assert bad.size == 0, f"{bad.size} differ, first gate {gate[bad[0]]!r}: {got[bad[0]]!r} vs {want[bad[0]]!r}"

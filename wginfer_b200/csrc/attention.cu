@@ -1076,7 +1076,7 @@ __global__ void __launch_bounds__(kThreads) attn_ref_kernel(const T *__restrict_
     }
     __syncthreads();
     mx = s_max;
-    for (int j = tid; j < nkeys; j += kThreads) sc[j] = exp_cr(__fsub_rn(sc[j], mx));
+    for (int j = tid; j < nkeys; j += kThreads) sc[j] = expf_glibc(__fsub_rn(sc[j], mx));
     __syncthreads();
     if (tid == 0) {  // sequential sum over every key (self_attention_cpu.cpp:70-74)
         float sum = 0.f;
@@ -1369,34 +1369,22 @@ extern "C" int wgb_self_attention(void *attn_val, const void *q, const void *k, 
 // allocation hook, and real-time threads that must not block in the driver.
 // wgb_self_attention_noalloc serves them with a fixed scratch array compiled
 // into this library instead of the lazily allocated workspace.
-#include <mutex>
-
 namespace wgb {
 namespace {
 
 constexpr size_t kStaticScratchBytes = 4u << 20;  // 4 MiB, held by every GPU that loads the library
 static __device__ __align__(256) unsigned char g_attn_static_scratch[kStaticScratchBytes];
 
-std::mutex g_static_mu;
-void *g_static_ptr[64];  // device address of the array, per device; set once
-
-// The array's name in host code is only a host-side stand-in; the device
-// address must be looked up with the device current.
+// The array's name in host code is only a host-side stand-in; its device
+// address is looked up on every call, with the caller's device current (the
+// lookup is cheap, and an address kept from an earlier call would be stale
+// after a cudaDeviceReset reloads the module).
 int static_scratch(void **out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "wgb_self_attention_noalloc: %s", cudaGetErrorString(e));
-    if (dev < 0 || dev >= 64) return set_error(WGB_ERR_INVALID_ARGUMENT, "device id %d", dev);
-    std::lock_guard<std::mutex> lk(g_static_mu);
-    if (g_static_ptr[dev] == nullptr) {
-        void *p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
-        if (e != cudaSuccess || p == nullptr)
-            return set_error(WGB_ERR_CUDA, "wgb_self_attention_noalloc: cudaGetSymbolAddress: %s",
-                             cudaGetErrorString(e));
-        g_static_ptr[dev] = p;
-    }
-    *out = g_static_ptr[dev];
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
+    if (e != cudaSuccess || p == nullptr)
+        return set_error(WGB_ERR_CUDA, "wgb_self_attention_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    *out = p;
     return WGB_OK;
 }
 
@@ -1421,9 +1409,10 @@ extern "C" int wgb_self_attention_noalloc(void *attn_val, const void *q, const v
         rc = wgb::static_scratch(&ws);
         if (rc) return rc;
     }
-    // Every scratch word the kernels read is written earlier in the same call
-    // (each key slice stores its max, sum and partial output before the
-    // combine reads them), so nothing needs clearing between calls.
+    // The scratch holds attn_ref_kernel's one score per key (REFERENCE
+    // numerics, caches longer than kRefSmemScores keys). Every score a CTA
+    // reads, sc[j] for j < nkeys, is written earlier in the same call, so
+    // nothing needs clearing between calls.
     return wgb_self_attention_ex(attn_val, q, k, v, dtype, seqlen, nhead, nkvhead, d, dv, total_len, scale, ws,
                                  need, stream);
 }

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "libm_expf.cuh"
 #include "wginfer_b200.h"
 
 namespace wgb {
@@ -88,13 +89,20 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// Correctly rounded (with overwhelming probability) single-precision
-// transcendentals evaluated in double precision. Used where results must
-// agree with a correctly rounding C library.
-__device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
+// Single-precision sin, cos and pow evaluated in double precision and rounded
+// once (correctly rounded with overwhelming probability). exp has its own
+// restatement of the C library's algorithm (libm_expf.cuh), which matches the
+// reference's std::exp(float) bit for bit.
 __device__ __forceinline__ float sin_cr(float x) { return (float)sin((double)x); }
 __device__ __forceinline__ float cos_cr(float x) { return (float)cos((double)x); }
 __device__ __forceinline__ float pow_cr(float b, float e) { return (float)pow((double)b, (double)e); }
+
+// rms_norm's 1 / sqrt(sum / n + eps), each operation rounded once
+// (rms_norm_cpu.cpp:18-19: std::sqrt of a float is the correctly rounded sqrtf).
+__device__ __forceinline__ float rms_scale(float sum, int n, float eps) {
+    const float mean = __fdiv_rn(sum, (float)n);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -9,7 +9,7 @@
 
 namespace wgb {
 
-enum Epi { EPI_STORE = DG_EPI_STORE, EPI_SWIGLU = DG_EPI_SWIGLU, EPI_ROPEKV = DG_EPI_ROPEKV };
+enum Epi { EPI_STORE = DG_EPI_STORE, EPI_SWIGLU = DG_EPI_SWIGLU, EPI_ROPEKV = DG_EPI_ROPEKV, EPI_ARGMAX = DG_EPI_ARGMAX };
 
 // Weight row pair g is rows (2g, 2g + 1) for every epilogue: the model stores
 // q/k rows with rotation partners (j, j + dh/2) of a head next to each other
@@ -80,7 +80,7 @@ __device__ __forceinline__ void epilogue(const DecodeGemvParams &p, int g, int r
         const float uu = Elem<T>::load(Elem<T>::store(s1));
         stf(reinterpret_cast<T *>(p.out), (size_t)m * p.ldo + g,
             __fdiv_rn(__fmul_rn(uu, gg), __fadd_rn(1.0f, expf(-gg))));
-    } else {
+    } else if (EPI == EPI_ROPEKV) {
         const int64_t pos = p.pos[m];
         const int half = p.dh >> 1;
         const int P = (p.nh + p.nkvh) * half;
@@ -122,7 +122,7 @@ __device__ __forceinline__ void epilogue_pre(const DecodeGemvParams &p, int g, i
         const float uu = Elem<T>::load(Elem<T>::store(s1));
         stf(reinterpret_cast<T *>(p.out), (size_t)m * p.ldo + g,
             __fdiv_rn(__fmul_rn(uu, gg), __fadd_rn(1.0f, expf(-gg))));
-    } else {
+    } else if (EPI == EPI_ROPEKV) {
         rope_kv_store<T>(p, g, r1ok, m, s0, s1, e.pos, e.cs);
     }
 }

@@ -15,6 +15,14 @@
 //                     of one q or k head: the rounded pair is rotated with
 //                     the host-built cos/sin table and written to q_rope or
 //                     straight into the K cache; v rows go to the V cache.
+//             ARGMAX- the lm_head of a decode step: logits stored as with
+//                     STORE, and each row's greedy token found on the way:
+//                     a CTA folds its outputs' (value, first index) keys
+//                     (argmax_key.cuh) in shared memory, merges them with one
+//                     global atomic per input row, and the CTA that finishes
+//                     last writes the tokens and advances the sequence
+//                     lengths (model.cpp:398-407), so no argmax launch and
+//                     no second pass over the 151936 logits follow.
 // Each warp owns two weight rows at a time (chosen by the epilogue's row map)
 // and a 1/KS slice of K; lanes stream 16-byte weight vectors with an L2
 // evict-first policy, several vectors in flight per lane. The grid is
@@ -31,6 +39,7 @@
 
 #include <atomic>
 
+#include "argmax_key.cuh"
 #include "common.cuh"
 #include "decode_common.cuh"
 #include "kernels.h"
@@ -60,6 +69,8 @@ __global__ void __launch_bounds__(256, (MT <= 2 ? 3 : 2)) decode_gemv_kernel(Dec
     __shared__ float s_scale[MT];
     __shared__ float s_part[8][MT];
     __shared__ float s_epi[8][MT][4];  // first block: bias (b0, b1) and residual (q0, q1) per warp and row
+    __shared__ unsigned long long s_key[MT];  // ARGMAX: this CTA's best key per input row
+    if (EPI == EPI_ARGMAX && threadIdx.x < MT) s_key[threadIdx.x] = 0ull;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rg = warp / KS, ks = warp % KS;
@@ -290,7 +301,17 @@ __global__ void __launch_bounds__(256, (MT <= 2 ? 3 : 2)) decode_gemv_kernel(Dec
                         s1 = acc[1][mm];
                     }
             }
-            if (blk == (int)blockIdx.x) {
+            if (EPI == EPI_ARGMAX) {
+                T *out = reinterpret_cast<T *>(p.out);
+                stf(out, (size_t)m * p.ldo + r0, s0);
+                unsigned long long k = key_or_zero(Elem<T>::load(Elem<T>::store(s0)), (uint32_t)r0);
+                if (r1ok) {
+                    stf(out, (size_t)m * p.ldo + r1, s1);
+                    const unsigned long long k1 = key_or_zero(Elem<T>::load(Elem<T>::store(s1)), (uint32_t)r1);
+                    k = k1 > k ? k1 : k;
+                }
+                if (k) atomicMax(&s_key[m], k);
+            } else if (blk == (int)blockIdx.x) {
                 EpiPre pre;
                 if (p.bias) {
                     pre.b0 = s_epi[warp][m][0];
@@ -307,6 +328,36 @@ __global__ void __launch_bounds__(256, (MT <= 2 ? 3 : 2)) decode_gemv_kernel(Dec
                 epilogue<T, EPI>(p, g, r0, r1, r1ok, m, s0, s1);
         }
         if (KS > 1) __syncthreads();  // red[] is rewritten by the next block
+    }
+    if (EPI == EPI_ARGMAX) {
+        __syncthreads();
+        if (threadIdx.x < M && s_key[threadIdx.x]) {
+            atomicMax(&p.amax_keys[threadIdx.x], s_key[threadIdx.x]);
+            __threadfence();
+        }
+        __syncthreads();
+        // the CTA that finishes last turns the keys into tokens
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const unsigned done = atomicAdd(p.amax_count, 1u);
+            if (done == gridDim.x - 1) {
+                __threadfence();
+                for (int m = 0; m < M; m++) {
+                    const unsigned long long key = atomicExch(&p.amax_keys[m], 0ull);
+                    const T *row0 = reinterpret_cast<const T *>(p.out) + (size_t)m * p.ldo;
+                    T x0;
+                    if constexpr (sizeof(T) == 4) {
+                        x0 = __ldcg(reinterpret_cast<const float *>(row0));
+                    } else {
+                        const unsigned short u = __ldcg(reinterpret_cast<const unsigned short *>(row0));
+                        memcpy(&x0, &u, 2);
+                    }
+                    p.tokens[m] = key_index(key, Elem<T>::load(x0));
+                    if (p.lens && p.lens[m] < p.maxlen) p.lens[m] += 1;
+                }
+                atomicExch(p.amax_count, 0u);
+            }
+        }
     }
 }
 
@@ -401,7 +452,7 @@ int dispatch(const DecodeGemvParams &p0, int pro, int epi, cudaStream_t s) {
                 "decode_gemv: K = %d is not a whole number of 16-byte vectors", p0.K);
     // more than 8 rows of bf16: one tensor-core GEMM over all rows (the RMS
     // prologue first materialised into p0.xn)
-    if (std::is_same<T, __nv_bfloat16>::value && p0.M0 > kMaxMT && (pro == PRO_PLAIN || p0.xn)) {
+    if (std::is_same<T, __nv_bfloat16>::value && p0.M0 > kMaxMT && epi != EPI_ARGMAX && (pro == PRO_PLAIN || p0.xn)) {
         DecodeGemvParams p = p0;
         p.M = p0.M0;
         if (pro == PRO_RMS) p.x = p0.xn;
@@ -431,7 +482,16 @@ int dispatch(const DecodeGemvParams &p0, int pro, int epi, cudaStream_t s) {
         else if (pro == PRO_RMS && epi == EPI_ROPEKV) rc = launch_mt<T, PRO_RMS, EPI_ROPEKV>(p, s);
         else if (pro == PRO_RMS && epi == EPI_STORE) rc = launch_mt<T, PRO_RMS, EPI_STORE>(p, s);
         else if (pro == PRO_PLAIN && epi == EPI_STORE) rc = launch_mt<T, PRO_PLAIN, EPI_STORE>(p, s);
-        else return set_error(WGB_ERR_UNSUPPORTED, "decode_gemv: prologue %d with epilogue %d", pro, epi);
+        else if (pro == PRO_RMS && epi == EPI_ARGMAX) {
+            // one launch covers every row (the keys are per row of this launch);
+            // the K split stays 1 (the lm_head has row blocks to fill the GPU)
+            WGB_REQUIRE(p0.M0 <= kMaxMT && !p0.bias && p0.amax_keys && p0.amax_count && p0.tokens,
+                        WGB_ERR_INVALID_ARGUMENT, "decode_gemv: argmax epilogue needs <= 8 rows, its key buffers, no bias");
+            if (p.M <= 1) rc = launch_one<T, 1, 1, PRO_RMS, EPI_ARGMAX>(p, s);
+            else if (p.M <= 2) rc = launch_one<T, 2, 1, PRO_RMS, EPI_ARGMAX>(p, s);
+            else if (p.M <= 4) rc = launch_one<T, 4, 1, PRO_RMS, EPI_ARGMAX>(p, s);
+            else rc = launch_one<T, 8, 1, PRO_RMS, EPI_ARGMAX>(p, s);
+        } else return set_error(WGB_ERR_UNSUPPORTED, "decode_gemv: prologue %d with epilogue %d", pro, epi);
         if (rc) return rc;
     }
     return WGB_OK;
@@ -455,6 +515,11 @@ template <typename T> void attrs_all() {
     attrs_mt<T, PRO_RMS, EPI_ROPEKV>();
     attrs_mt<T, PRO_RMS, EPI_STORE>();
     attrs_mt<T, PRO_PLAIN, EPI_STORE>();
+    const int lim = 200 * 1024;
+    cudaFuncSetAttribute(decode_gemv_kernel<T, 1, 1, PRO_RMS, EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(decode_gemv_kernel<T, 2, 1, PRO_RMS, EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(decode_gemv_kernel<T, 4, 1, PRO_RMS, EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(decode_gemv_kernel<T, 8, 1, PRO_RMS, EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
 }
 
 }  // namespace

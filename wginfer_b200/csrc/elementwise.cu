@@ -19,14 +19,14 @@ struct AddOp {
 
 // src/ops/swiglu/cpu/swiglu_cpu.cpp:11 evaluates up * gate / (1 + exp(-gate))
 // with the product and the quotient each rounded once; REFERENCE keeps that
-// literally (exp correctly rounded). FAST uses the hardware exp2-based __expf
+// literally, with the C library's expf restated (libm_expf.cuh). FAST uses the hardware exp2-based __expf
 // and the approximate quotient __fdividef (a few ulp: relative error below
 // 1e-6 for |gate| < 20, and 0 instead of a denormal once 1 + exp(-gate)
 // passes 2^126): at bf16 the IEEE division and accurate expf made the op
 // instruction-bound, well short of HBM bandwidth.
 template <bool kRef> struct SwigluOp {
     __device__ __forceinline__ float operator()(float g, float u) const {
-        if (kRef) return __fdiv_rn(__fmul_rn(u, g), __fadd_rn(1.0f, exp_cr(-g)));
+        if (kRef) return __fdiv_rn(__fmul_rn(u, g), __fadd_rn(1.0f, expf_glibc(-g)));
         return __fdividef(u * g, 1.0f + __expf(-g));
     }
 };

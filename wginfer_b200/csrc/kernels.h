@@ -73,8 +73,17 @@ struct DecodeGemvParams {
     size_t tc_ws_bytes;
     unsigned *tc_cnt;
     int tc_cnt_n;
+    // epilogue ARGMAX (the lm_head of a decode step): the logits are stored
+    // as with STORE, and each CTA folds its rows' (value, index) keys into
+    // amax_keys[m] (zero between launches); the CTA that finishes last writes
+    // tokens[m] = argmax of row m, advances lens[m] (up to maxlen) and clears
+    // the keys and amax_count
+    unsigned long long *amax_keys;  // [M0]
+    unsigned *amax_count;
+    int64_t *tokens, *lens;
+    int64_t maxlen;
 };
-enum { DG_PRO_PLAIN = 0, DG_PRO_RMS = 1, DG_EPI_STORE = 0, DG_EPI_SWIGLU = 1, DG_EPI_ROPEKV = 2 };
+enum { DG_PRO_PLAIN = 0, DG_PRO_RMS = 1, DG_EPI_STORE = 0, DG_EPI_SWIGLU = 1, DG_EPI_ROPEKV = 2, DG_EPI_ARGMAX = 3 };
 int decode_gemv(wginferDataType_t dtype, const DecodeGemvParams &p, int pro, int epi, cudaStream_t s);
 void decode_gemv_prepare();  // raises shared-memory limits; call outside graph capture
 
@@ -84,5 +93,24 @@ void decode_gemv_prepare();  // raises shared-memory limits; call outside graph 
 bool tc_gemm_ok(const DecodeGemvParams &p);
 int tc_gemm(const DecodeGemvParams &p, int epi, cudaStream_t s);
 void tc_gemm_prepare();
+
+// REFERENCE-numerics decode kernels for up to kRefChainMaxM input rows
+// (ref_decode.cu): the projections with every output one sequential f32
+// chain over K (linear_cpu.cpp:86-99), weights streamed ahead of the chains
+// into shared memory; prologue RMS and the STORE / SWIGLU / ROPEKV / ARGMAX
+// epilogues as in DecodeGemvParams (bias starts the chain). ref_chain_ok:
+// whether ref_chain_gemv takes these arguments (else use linear_forward).
+constexpr int kRefChainMaxM = 4;
+bool ref_chain_ok(wginferDataType_t dtype, const DecodeGemvParams &p);
+int ref_chain_gemv(wginferDataType_t dtype, const DecodeGemvParams &p, int pro, int epi, cudaStream_t s);
+// Decode attention over per-sequence caches in the reference's order
+// (self_attention_cpu.cpp:37-89) for caches of up to ref_attn_max_len()
+// positions; false from ref_attn_decode_ok: use attn_decode.
+bool ref_attn_decode_ok(wginferDataType_t dtype, int nh, int nkvh, int dh, int maxlen, const void *kcache,
+                        const void *vcache, size_t seq_stride);
+int ref_attn_decode(wginferDataType_t dtype, void *out, const void *q, const void *kcache, const void *vcache,
+                    size_t seq_stride, const int64_t *lens, int B, int nh, int nkvh, int dh, int maxlen, float scale,
+                    cudaStream_t s);
+void ref_decode_prepare();  // raises shared-memory limits; call outside graph capture
 
 }  // namespace wgb

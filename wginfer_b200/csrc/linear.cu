@@ -158,6 +158,27 @@ template <typename T>
 int launch_linear(T *out, const T *x, const T *w, const T *bias, const T *res, size_t M, size_t N, size_t K,
                   bool ref, cudaStream_t s) {
     constexpr int V = Vec16<T>::N;
+    if (ref && M <= (size_t)kRefChainMaxM) {
+        // a few rows: one chain per lane, weights streamed ahead (ref_decode.cu)
+        DecodeGemvParams p{};
+        p.w = w;
+        p.x = x;
+        p.M0 = (int)M;
+        p.N = (int)N;
+        p.K = (int)K;
+        p.out = out;
+        p.ldo = (int)N;
+        p.bias = bias;
+        p.res = res;
+        p.err = dev_error_ptr();
+        const wginferDataType_t dt = std::is_same<T, float>::value    ? WGINFER_DTYPE_F32
+                                     : std::is_same<T, __half>::value ? WGINFER_DTYPE_F16
+                                                                      : WGINFER_DTYPE_BF16;
+        if (ref_chain_ok(dt, p)) {
+            ref_decode_prepare();
+            return ref_chain_gemv(dt, p, DG_PRO_PLAIN, DG_EPI_STORE, s);
+        }
+    }
     if (ref) {
         // one input row: one chain per thread; otherwise eight chains per thread
         const int mt = M == 1 ? 1 : kRefMT;

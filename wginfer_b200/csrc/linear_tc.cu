@@ -30,6 +30,7 @@
 #include "common.cuh"
 #include "decode_common.cuh"
 #include "kernels.h"
+#include "tma.cuh"
 
 namespace wgb {
 namespace {
@@ -622,6 +623,35 @@ bool make_map(CUtensorMap *tm, const void *base, int rows, int K, int box_rows) 
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+}  // namespace
+
+bool tma_map_rows(CUtensorMap *tm, const void *base, int es, int rows, int cols, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || (es != 2 && es != 4)) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * (cuuint64_t)es};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(tm, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(base),
+              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool tma_map_row_stages(CUtensorMap *tm, const void *base, int es, int rows, int cols, int box_rows, int stages) {
+    EncodeTiledFn fn = encode_fn();
+    const int blk = es == 2 || es == 4 ? 128 / es : 0;
+    if (!fn || !blk || cols % blk) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)blk, (cuuint64_t)rows, (cuuint64_t)(cols / blk)};
+    cuuint64_t strides[2] = {(cuuint64_t)cols * (cuuint64_t)es, 128};
+    cuuint32_t box[3] = {(cuuint32_t)blk, (cuuint32_t)box_rows, (cuuint32_t)stages};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(tm, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void *>(base),
+              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+namespace {
 
 // Input rows per tile: the smallest power of two >= M up to 256 (the MMA's
 // largest N; fewer re-reads of the weight tile), then halved (down to 16)

@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(256) swiglu_rows_kernel(T *__restrict__ act, c
     for (size_t i = (size_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (size_t)gridDim.x * 256) {
         const size_t t = i / di, j = i - t * di;  // gate and up rows are interleaved
         const float g = ldf(gu, t * 2 * di + 2 * j), u = ldf(gu, t * 2 * di + 2 * j + 1);
-        const float e = kRef ? exp_cr(-g) : expf(-g);
+        const float e = kRef ? expf_glibc(-g) : expf(-g);
         stf(act, i, __fdiv_rn(__fmul_rn(u, g), __fadd_rn(1.0f, e)));
     }
 }
@@ -147,6 +147,8 @@ struct wgbQwen2Model {
     void *attn_ws;
     float *tc_ws;      // [kTcSites] split-K accumulators (zero between launches)
     unsigned *tc_cnt;  // [kTcSites][kTcCounters] arrival counters (zero between launches)
+    unsigned long long *amax_keys;  // [max_batch] fused lm_head + argmax keys (zero between launches)
+    unsigned *amax_count;           // its CTA arrival counter (zero between launches)
     size_t attn_ws_bytes;
     int64_t *h_pinned;  // pinned host staging for token ids
     unsigned long long sample_seed = 0, sample_step = 0;  // device sampler: seed, draws so far
@@ -370,6 +372,104 @@ int run_layer_fast(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t to
     return rc;
 }
 
+// Whether a decode step of B sequences takes the REFERENCE chain kernels
+// (ref_decode.cu): up to kRefChainMaxM rows, caches the decode attention holds.
+bool ref_decode_fast_ok(const wgbQwen2Model *M, int B) {
+    const wgbQwen2Meta &m = M->m;
+    if (B > kRefChainMaxM) return false;
+    if (!ref_attn_decode_ok(M->dt, (int)m.nh, (int)m.nkvh, (int)m.dh, (int)m.maxseq, M->kc, M->vc, M->seq_stride))
+        return false;
+    DecodeGemvParams p{};
+    p.M0 = B;
+    p.w = M->L[0].down_w;
+    p.x = M->act;
+    p.N = (int)m.hs;
+    p.K = (int)m.di;  // the longest rows; the other projections have K = hs or nh * dh
+    if (!ref_chain_ok(M->dt, p)) return false;
+    p.K = (int)m.hs;
+    if (!ref_chain_ok(M->dt, p)) return false;
+    p.K = (int)(m.nh * m.dh);
+    return ref_chain_ok(M->dt, p);
+}
+
+// One decode layer for B <= kRefChainMaxM sequences in REFERENCE numerics:
+// the op sequence of run_layer_ref (model.cpp:243-328) in five launches
+// chained by programmatic dependent launch, every sum in the reference's
+// order (ref_decode.cu): rms_norm + q/k/v + bias + RoPE + K/V append;
+// attention; o + residual; rms_norm + gate/up + SwiGLU; down + residual.
+int run_layer_ref_decode(wgbQwen2Model *M, size_t l, int B) {
+    const wgbQwen2Meta &m = M->m;
+    cudaStream_t s = M->stream;
+    const LayerW &w = M->L[l];
+    const int hs = (int)m.hs, di = (int)m.di;
+    int rc;
+    DecodeGemvParams p{};
+    p.M0 = B;
+    p.err = dev_error_ptr();
+    p.eps = m.epsilon;
+    p.w = w.qkv_w;
+    p.x = M->x;
+    p.N = (int)M->nq();
+    p.K = hs;
+    p.norm_w = w.attn_norm;
+    p.bias = w.qkv_b;
+    p.pos = M->lens;
+    p.table = M->rope_table;
+    p.q_out = M->qr;
+    p.kc = M->layer_k(l);
+    p.vc = M->layer_v(l);
+    p.seq_stride = M->seq_stride;
+    p.nh = (int)m.nh;
+    p.nkvh = (int)m.nkvh;
+    p.dh = (int)m.dh;
+    p.maxseq = (int)m.maxseq;
+    p.prefill_seq = -1;
+    if ((rc = ref_chain_gemv(M->dt, p, DG_PRO_RMS, DG_EPI_ROPEKV, s))) return rc;
+    WGB_TRACE("ref qkv+rms+rope+kv");
+    if ((rc = ref_attn_decode(M->dt, M->att, M->qr, M->layer_k(l), M->layer_v(l), M->seq_stride, M->lens, B,
+                              (int)m.nh, (int)m.nkvh, (int)m.dh, (int)m.maxseq, 1.0f / sqrtf((float)m.dh), s)))
+        return rc;
+    WGB_TRACE("ref attention");
+    DecodeGemvParams o{};
+    o.M0 = B;
+    o.err = p.err;
+    o.w = w.o_w;
+    o.x = M->att;
+    o.N = hs;
+    o.K = (int)(m.nh * m.dh);
+    o.out = M->x;
+    o.ldo = hs;
+    o.res = M->x;
+    if ((rc = ref_chain_gemv(M->dt, o, DG_PRO_PLAIN, DG_EPI_STORE, s))) return rc;
+    WGB_TRACE("ref o+residual");
+    DecodeGemvParams g{};
+    g.M0 = B;
+    g.err = p.err;
+    g.w = w.gu_w;
+    g.x = M->x;
+    g.N = 2 * di;
+    g.K = hs;
+    g.norm_w = w.mlp_norm;
+    g.eps = m.epsilon;
+    g.out = M->act;
+    g.ldo = di;
+    if ((rc = ref_chain_gemv(M->dt, g, DG_PRO_RMS, DG_EPI_SWIGLU, s))) return rc;
+    WGB_TRACE("ref gate_up+rms+swiglu");
+    DecodeGemvParams d{};
+    d.M0 = B;
+    d.err = p.err;
+    d.w = w.down_w;
+    d.x = M->act;
+    d.N = hs;
+    d.K = di;
+    d.out = M->x;
+    d.ldo = hs;
+    d.res = M->x;
+    rc = ref_chain_gemv(M->dt, d, DG_PRO_PLAIN, DG_EPI_STORE, s);
+    WGB_TRACE("ref down+residual");
+    return rc;
+}
+
 int run_layer(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t total_len, bool ref) {
     return ref ? run_layer_ref(M, l, T, prefill_seq, total_len) : run_layer_fast(M, l, T, prefill_seq, total_len);
 }
@@ -407,8 +507,56 @@ int decode_body(wgbQwen2Model *M, int B, bool ref) {
 
     if ((rc = wgb_embedding(M->x, M->tokens, M->in_embed, M->dt, B, m.hs, m.voc, s))) return rc;
     WGB_TRACE("embedding");
+    if (ref && ref_decode_fast_ok(M, B)) {
+        for (size_t l = 0; l < m.nlayer; l++)
+            if ((rc = run_layer_ref_decode(M, l, B))) return rc;
+        // final rms_norm + lm_head + greedy argmax + lengths advanced, one launch
+        DecodeGemvParams p{};
+        p.M0 = B;
+        p.err = dev_error_ptr();
+        p.w = M->out_embed;
+        p.x = M->x;
+        p.N = (int)m.voc;
+        p.K = (int)m.hs;
+        p.norm_w = M->out_norm;
+        p.eps = m.epsilon;
+        p.out = M->logits;
+        p.ldo = (int)m.voc;
+        p.amax_keys = M->amax_keys;
+        p.amax_count = M->amax_count;
+        p.tokens = M->tokens;
+        p.lens = M->lens;
+        p.maxlen = (int64_t)m.maxseq;
+        rc = ref_chain_gemv(M->dt, p, DG_PRO_RMS, DG_EPI_ARGMAX, s);
+        WGB_TRACE("ref lm_head+rms+argmax+advance");
+        return rc;
+    }
     for (size_t l = 0; l < m.nlayer; l++)
         if ((rc = run_layer(M, l, B, -1, 0, ref))) return rc;
+    if (!ref && B <= 8) {
+        // final rms_norm + lm_head + greedy argmax + lengths advanced, one launch
+        DecodeGemvParams p{};
+        p.M0 = B;
+        p.err = dev_error_ptr();
+        p.w = M->out_embed;
+        p.x = M->x;
+        p.N = (int)m.voc;
+        p.K = (int)m.hs;
+        p.groups = (int)(m.voc + 1) / 2;
+        p.norm_w = M->out_norm;
+        p.eps = m.epsilon;
+        p.out = M->logits;
+        p.ldo = (int)m.voc;
+        p.xn = M->xn;
+        p.amax_keys = M->amax_keys;
+        p.amax_count = M->amax_count;
+        p.tokens = M->tokens;
+        p.lens = M->lens;
+        p.maxlen = (int64_t)m.maxseq;
+        rc = decode_gemv(M->dt, p, DG_PRO_RMS, DG_EPI_ARGMAX, s);
+        WGB_TRACE("lm_head_gemv+rms+argmax+advance");
+        return rc;
+    }
     if ((rc = lm_head(M, M->x, B, M->logits, ref))) return rc;
     WGB_TRACE("lm_head_gemv+rms");
     // the greedy tokens, and every sequence one position longer
@@ -564,6 +712,8 @@ int wgb_qwen2_create(const wgbQwen2Meta *meta, int device, int max_batch, wgbQwe
     items.push_back({&M->attn_ws, M->attn_ws_bytes});
     items.push_back({(void **)&M->tc_ws, kTcSites * kTcWsBytes});
     items.push_back({(void **)&M->tc_cnt, (size_t)kTcSites * kTcCounters * sizeof(unsigned)});
+    items.push_back({(void **)&M->amax_keys, (size_t)max_batch * sizeof(unsigned long long)});
+    items.push_back({(void **)&M->amax_count, sizeof(unsigned)});
 
     size_t total = 0;
     for (auto &it : items) total += align256(it.bytes);
@@ -595,6 +745,7 @@ int wgb_qwen2_create(const wgbQwen2Meta *meta, int device, int max_batch, wgbQwe
     if (!rc && cudaStreamSynchronize(M->stream) != cudaSuccess) rc = cuda_err("create sync");
     attn_prepare();
     decode_gemv_prepare();
+    ref_decode_prepare();
 
     dev_error_ptr();  // resolve the error-word address outside any graph capture
     M->h_lens.assign(max_batch, 0);

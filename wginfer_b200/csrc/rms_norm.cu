@@ -16,11 +16,6 @@
 namespace wgb {
 namespace {
 
-__device__ __forceinline__ float rms_scale(float sum, int n, float eps) {
-    float mean = __fdiv_rn(sum, (float)n);
-    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-}
-
 template <typename T, int VPL>
 __global__ void __launch_bounds__(256) rms_warp_kernel(T *__restrict__ out, const T *__restrict__ in,
                                                        const T *__restrict__ w, int M, int N, float eps) {
