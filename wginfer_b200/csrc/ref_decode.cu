@@ -102,7 +102,7 @@ template <> __device__ __forceinline__ void chain_vec<__nv_bfloat16>(float &acc,
     const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
     for (int q = 0; q < 4; q++)
-        asm("{\n .reg .b16 xl, xh, wl, wh;\n mov.b32 {xl, xh}, %1;\n mov.b32 {wl, wh}, %2;\n"
+        asm volatile("{\n .reg .b16 xl, xh, wl, wh;\n mov.b32 {xl, xh}, %1;\n mov.b32 {wl, wh}, %2;\n"
             " fma.rn.f32.bf16 %0, xl, wl, %0;\n fma.rn.f32.bf16 %0, xh, wh, %0;\n}"
             : "+f"(acc)
             : "r"(xs[q]), "r"(ws[q]));
@@ -111,7 +111,7 @@ template <> __device__ __forceinline__ void chain_vec<__half>(float &acc, const 
     const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
     for (int q = 0; q < 4; q++)
-        asm("{\n .reg .b16 xl, xh, wl, wh;\n mov.b32 {xl, xh}, %1;\n mov.b32 {wl, wh}, %2;\n"
+        asm volatile("{\n .reg .b16 xl, xh, wl, wh;\n mov.b32 {xl, xh}, %1;\n mov.b32 {wl, wh}, %2;\n"
             " fma.rn.f32.f16 %0, xl, wl, %0;\n fma.rn.f32.f16 %0, xh, wh, %0;\n}"
             : "+f"(acc)
             : "r"(xs[q]), "r"(ws[q]));
@@ -144,6 +144,32 @@ template <typename T> __device__ __forceinline__ void stage_copy(T *dst, const T
     constexpr int V = 16 / sizeof(T);
     for (int i = threadIdx.x; i < n / V; i += blockDim.x) __pipeline_memcpy_async(dst + i * V, src + i * V, 16);
     __pipeline_commit();
+}
+
+template <int MT> struct ChainAcc {
+    float v[MT];
+};
+
+// One full stage (128 bytes of each row) of chain steps: the stage's 16-byte
+// operands are all loaded first, then its steps run (loads and steps are
+// volatile asm, so the compiler keeps that order). wr: this lane's weight row
+// in the ring (16-byte chunk c at c ^ sw); xr: input row 0 at this stage;
+// xrow: bytes between input rows.
+template <typename T, int MT>
+__device__ __forceinline__ ChainAcc<MT> chain_stage(ChainAcc<MT> acc, uint32_t wr, uint32_t xr, int sw, uint32_t xrow) {
+    constexpr int VPS = kRcStageBytes / 16;
+    uint4 wv[VPS], xv[MT][VPS];
+#pragma unroll
+    for (int v = 0; v < VPS; v++) {
+        wv[v] = lds128(wr + (uint32_t)((v ^ sw) << 4));
+#pragma unroll
+        for (int m = 0; m < MT; m++) xv[m][v] = lds128(xr + m * xrow + (uint32_t)(v * 16));
+    }
+#pragma unroll
+    for (int v = 0; v < VPS; v++)
+#pragma unroll
+        for (int m = 0; m < MT; m++) chain_vec<T>(acc.v[m], xv[m][v], wv[v]);
+    return acc;
 }
 
 // tmW: tma_map_row_stages view of the weights with J-stage boxes (J > 1), or
@@ -221,17 +247,20 @@ __global__ void __launch_bounds__(32 * kRcMaxWarps)
         // rms_norm_cpu.cpp:11-19: sum += v * v in index order, then
         // 1 / sqrt(sum / N + eps); one lane per input row
         if (threadIdx.x < M) {
-            const uint4 *xr = reinterpret_cast<const uint4 *>(xs + (size_t)threadIdx.x * K);
+            const uint32_t xr = smem_u32(xs + (size_t)threadIdx.x * K);
             float sum = 0.f;
             int v = 0;
             for (; v + 4 <= K / V; v += 4) {  // four vectors loaded, then their chain steps
                 uint4 q[4];
 #pragma unroll
-                for (int u = 0; u < 4; u++) q[u] = xr[v + u];
+                for (int u = 0; u < 4; u++) q[u] = lds128(xr + (uint32_t)((v + u) * 16));
 #pragma unroll
                 for (int u = 0; u < 4; u++) chain_vec<T>(sum, q[u], q[u]);
             }
-            for (; v < K / V; v++) chain_vec<T>(sum, xr[v], xr[v]);
+            for (; v < K / V; v++) {
+                const uint4 q = lds128(xr + (uint32_t)(v * 16));
+                chain_vec<T>(sum, q, q);
+            }
             s_scale[threadIdx.x] = rms_scale(sum, K, p.eps);
         }
         __syncthreads();
@@ -245,59 +274,63 @@ __global__ void __launch_bounds__(32 * kRcMaxWarps)
     }
 
     const T *bias = reinterpret_cast<const T *>(p.bias);
+    const uint32_t ring_s = smem_u32(ring), xs_s = smem_u32(xs);
     int t = 0;
     bool failed = false;
     for (int bi = 0; bi < myblocks && !failed; bi++) {
         const int row = (first + bi * step) * kRcLanes + lane;
         const bool live = row < N;
         const float b0 = (bias && live) ? ldf(bias, row) : 0.f;
-        float acc[MT];
+        ChainAcc<MT> acc;
 #pragma unroll
-        for (int m = 0; m < MT; m++) acc[m] = __fadd_rn(0.f, b0);
-        for (int bx = 0; bx < nbox; bx++, t++) {
+        for (int m = 0; m < MT; m++) acc.v[m] = __fadd_rn(0.f, b0);
+        // boxes of whole stages (no per-stage test in this loop: a branch
+        // there cost 2 of the 8 cycles per chain step)
+        const int full_st = K / KT;
+        const int nbox_main = (full_st + J - 1) / J;
+        for (int bx = 0; bx < nbox_main; bx++, t++) {
             const int slot = t % ns;
             const bool ok = mbar_wait(&bar[slot], (unsigned)((t / ns) & 1), kRcWaitCycles);
             if (__any_sync(0xffffffffu, !ok)) {
                 failed = true;
                 break;
             }
-            for (int s = bx * J; s < min(nst, bx * J + J); s++) {
-                // this lane's row of the stage; 16-byte chunk c sits at c ^ (lane % 8)
-                const unsigned char *wr =
-                    ring + (size_t)slot * slot_bytes + (s - bx * J) * kRcStage + lane * kRcStageBytes;
-                const int sw = lane & 7;
-                const int k0 = s * KT, nv = min(KT, K - k0) / V;
-                if (nv == KT / V) {
-                    // the stage's operands first, then its chain steps
-                    uint4 wv[KT / V], xv[MT][KT / V];
-#pragma unroll
-                    for (int v = 0; v < KT / V; v++) {
-                        wv[v] = *reinterpret_cast<const uint4 *>(wr + ((v ^ sw) << 4));
-#pragma unroll
-                        for (int m = 0; m < MT; m++) xv[m][v] = *reinterpret_cast<const uint4 *>(xs + (size_t)m * K + k0 + v * V);
-                    }
-#pragma unroll
-                    for (int v = 0; v < KT / V; v++)
-#pragma unroll
-                        for (int m = 0; m < MT; m++) chain_vec<T>(acc[m], xv[m][v], wv[v]);
-                } else {
-                    for (int v = 0; v < nv; v++) {
-                        const uint4 wv = *reinterpret_cast<const uint4 *>(wr + ((v ^ sw) << 4));
-#pragma unroll
-                        for (int m = 0; m < MT; m++)
-                            chain_vec<T>(acc[m], *reinterpret_cast<const uint4 *>(xs + (size_t)m * K + k0 + v * V), wv);
-                    }
-                }
-            }
+            const uint32_t wbox = ring_s + (uint32_t)(slot * slot_bytes + lane * kRcStageBytes);
+            const int s1 = min(full_st, bx * J + J);
+            for (int s = bx * J; s < s1; s++)
+                acc = chain_stage<T, MT>(acc, wbox + (uint32_t)((s - bx * J) * kRcStage),
+                                         xs_s + (uint32_t)(s * KT * (int)sizeof(T)), lane & 7,
+                                         (uint32_t)(K * (int)sizeof(T)));
             __syncwarp();  // every lane is done with this slot before it is refilled
             if (issued < ntiles) issue(issued++);
+        }
+        if (!failed && full_st < nst) {
+            // the ragged last stage (K not a whole number of stages: one-stage boxes)
+            const int slot = t % ns;
+            const bool ok = mbar_wait(&bar[slot], (unsigned)((t / ns) & 1), kRcWaitCycles);
+            if (__any_sync(0xffffffffu, !ok)) {
+                failed = true;
+            } else {
+                const uint32_t wr = ring_s + (uint32_t)(slot * slot_bytes + lane * kRcStageBytes);
+                const uint32_t xr = xs_s + (uint32_t)(full_st * KT * (int)sizeof(T));
+                const int nv = (K - full_st * KT) / V;
+                for (int v = 0; v < nv; v++) {
+                    const uint4 wv = lds128(wr + (uint32_t)((v ^ (lane & 7)) << 4));
+#pragma unroll
+                    for (int m = 0; m < MT; m++)
+                        chain_vec<T>(acc.v[m], lds128(xr + (uint32_t)((m * K + v * V) * (int)sizeof(T))), wv);
+                }
+                __syncwarp();
+                if (issued < ntiles) issue(issued++);
+                t++;
+            }
         }
         if (failed) break;
         // epilogue of this row block
 #pragma unroll
         for (int m = 0; m < MT; m++) {
             if (m >= M) break;
-            const float a = acc[m];
+            const float a = acc.v[m];
             if (EPI == DG_EPI_STORE) {
                 if (live) {
                     const size_t i = (size_t)m * p.ldo + row;
