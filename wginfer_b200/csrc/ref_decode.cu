@@ -173,12 +173,14 @@ __device__ __forceinline__ ChainAcc<MT> chain_stage(ChainAcc<MT> acc, uint32_t w
 }
 
 // tmW: tma_map_row_stages view of the weights with J-stage boxes (J > 1), or
-// the tma_map_rows view with one-stage boxes (J == 1); ns ring slots per warp
-template <typename T, int MT, int PRO, int EPI>
+// the tma_map_rows view with one-stage boxes (J == 1); ns ring slots per warp.
+// J is a template parameter so that a box's stages are one unrolled block of
+// straight-line code (a runtime-bounded stage loop cost 1.3 cycles per chain
+// step).
+template <typename T, int MT, int PRO, int EPI, int J>
 __global__ void __launch_bounds__(32 * kRcMaxWarps)
-    ref_chain_kernel(const __grid_constant__ CUtensorMap tmW, DecodeGemvParams p, int ns, int J) {
+    ref_chain_kernel(const __grid_constant__ CUtensorMap tmW, DecodeGemvParams p, int ns) {
     constexpr int V = 16 / sizeof(T), KT = kRcStageBytes / sizeof(T);
-    constexpr bool kExact = sizeof(T) == 2;
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ float s_scale[MT];
     const int nw = blockDim.x >> 5;
@@ -284,11 +286,13 @@ __global__ void __launch_bounds__(32 * kRcMaxWarps)
         ChainAcc<MT> acc;
 #pragma unroll
         for (int m = 0; m < MT; m++) acc.v[m] = __fadd_rn(0.f, b0);
-        // boxes of whole stages (no per-stage test in this loop: a branch
-        // there cost 2 of the 8 cycles per chain step)
+        // boxes of J whole stages (no per-stage test in this loop: a branch
+        // there cost 2 of the 8 cycles per chain step), then a box of fewer
+        // stages, then the ragged stage (one-stage boxes only)
         const int full_st = K / KT;
-        const int nbox_main = (full_st + J - 1) / J;
-        for (int bx = 0; bx < nbox_main; bx++, t++) {
+        const int nfull = full_st / J;
+        const uint32_t xrow = (uint32_t)(K * (int)sizeof(T));
+        for (int bx = 0; bx < nfull; bx++, t++) {
             const int slot = t % ns;
             const bool ok = mbar_wait(&bar[slot], (unsigned)((t / ns) & 1), kRcWaitCycles);
             if (__any_sync(0xffffffffu, !ok)) {
@@ -296,13 +300,28 @@ __global__ void __launch_bounds__(32 * kRcMaxWarps)
                 break;
             }
             const uint32_t wbox = ring_s + (uint32_t)(slot * slot_bytes + lane * kRcStageBytes);
-            const int s1 = min(full_st, bx * J + J);
-            for (int s = bx * J; s < s1; s++)
-                acc = chain_stage<T, MT>(acc, wbox + (uint32_t)((s - bx * J) * kRcStage),
-                                         xs_s + (uint32_t)(s * KT * (int)sizeof(T)), lane & 7,
-                                         (uint32_t)(K * (int)sizeof(T)));
+            const uint32_t xbox = xs_s + (uint32_t)(bx * J * KT * (int)sizeof(T));
+#pragma unroll
+            for (int j = 0; j < J; j++)
+                acc = chain_stage<T, MT>(acc, wbox + (uint32_t)(j * kRcStage),
+                                         xbox + (uint32_t)(j * KT * (int)sizeof(T)), lane & 7, xrow);
             __syncwarp();  // every lane is done with this slot before it is refilled
             if (issued < ntiles) issue(issued++);
+        }
+        if (!failed && nfull * J < full_st) {
+            const int slot = t % ns;
+            const bool ok = mbar_wait(&bar[slot], (unsigned)((t / ns) & 1), kRcWaitCycles);
+            if (__any_sync(0xffffffffu, !ok)) {
+                failed = true;
+            } else {
+                const uint32_t wbox = ring_s + (uint32_t)(slot * slot_bytes + lane * kRcStageBytes);
+                for (int s = nfull * J; s < full_st; s++)
+                    acc = chain_stage<T, MT>(acc, wbox + (uint32_t)((s - nfull * J) * kRcStage),
+                                             xs_s + (uint32_t)(s * KT * (int)sizeof(T)), lane & 7, xrow);
+                __syncwarp();
+                if (issued < ntiles) issue(issued++);
+                t++;
+            }
         }
         if (!failed && full_st < nst) {
             // the ragged last stage (K not a whole number of stages: one-stage boxes)
@@ -398,15 +417,23 @@ __global__ void __launch_bounds__(32 * kRcMaxWarps)
 // together: one CTA per SM at most, see rc_plan.)
 
 template <typename T, int MT, int PRO, int EPI> void rc_set_attr() {
-    if (cudaFuncSetAttribute(ref_chain_kernel<T, MT, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    // the launch reports what is wrong if an attribute is refused
+    if (cudaFuncSetAttribute(ref_chain_kernel<T, MT, PRO, EPI, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kSmemLimit) != cudaSuccess)
-        cudaGetLastError();  // the launch then reports what is wrong
+        cudaGetLastError();
+    if (cudaFuncSetAttribute(ref_chain_kernel<T, MT, PRO, EPI, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemLimit) != cudaSuccess)
+        cudaGetLastError();
+    if (cudaFuncSetAttribute(ref_chain_kernel<T, MT, PRO, EPI, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemLimit) != cudaSuccess)
+        cudaGetLastError();
 }
 
 // Launch plan: warps per CTA (one for narrow projections, so more SMs pull
 // weights; four when there are many row blocks, sharing one copy of the
 // input rows), stages per box J (8 for one warp, 4 for four; 1 when K is
-// not a whole number of stages) and ring slots per warp (up to 5, as many as
+// not a whole number of stages or is shorter than a box; J is one of 1, 4,
+// 8, the compiled variants) and ring slots per warp (up to 5, as many as
 // one CTA per SM leaves room for, at least 2). The grid never exceeds one
 // CTA per SM: every CTA is resident at once, and extra row blocks are
 // walked by the persistent loop.
@@ -422,14 +449,14 @@ RcPlan rc_plan(int N, int K, int mt, size_t es) {
     pl.nw = nblocks >= 2 * sm_count() ? kRcMaxWarps : 1;
     for (;;) {
         pl.J = K % KT ? 1 : (pl.nw == 1 ? 8 : 4);
-        if (pl.J > nst) pl.J = nst;
+        if (pl.J > nst) pl.J = nst >= 4 ? 4 : 1;
         const int want = pl.J == 1 ? kRcMaxSlots : 5;
         for (pl.ns = want; pl.ns > 2 && rc_smem_bytes(pl.nw, pl.ns, pl.J, mt, K, es) > kSmemLimit; pl.ns--) {
         }
         if (rc_smem_bytes(pl.nw, pl.ns, pl.J, mt, K, es) <= kSmemLimit || pl.nw == 1) break;
         pl.nw--;
     }
-    while (pl.J > 1 && rc_smem_bytes(pl.nw, pl.ns, pl.J, mt, K, es) > kSmemLimit) pl.J /= 2;
+    while (pl.J > 1 && rc_smem_bytes(pl.nw, pl.ns, pl.J, mt, K, es) > kSmemLimit) pl.J = pl.J == 8 ? 4 : 1;
     pl.smem = rc_smem_bytes(pl.nw, pl.ns, pl.J, mt, K, es);
     return pl;
 }
@@ -454,7 +481,10 @@ template <typename T, int MT, int PRO, int EPI> int launch_rc(const DecodeGemvPa
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, ref_chain_kernel<T, MT, PRO, EPI>, tm, p, pl.ns, pl.J);
+    cudaError_t e;
+    if (pl.J == 8) e = cudaLaunchKernelEx(&cfg, ref_chain_kernel<T, MT, PRO, EPI, 8>, tm, p, pl.ns);
+    else if (pl.J == 4) e = cudaLaunchKernelEx(&cfg, ref_chain_kernel<T, MT, PRO, EPI, 4>, tm, p, pl.ns);
+    else e = cudaLaunchKernelEx(&cfg, ref_chain_kernel<T, MT, PRO, EPI, 1>, tm, p, pl.ns);
     if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "ref_chain_gemv: %s", cudaGetErrorString(e));
     return check_launch("ref_chain_gemv");
 }
@@ -510,7 +540,7 @@ __global__ void __launch_bounds__(kRaThreads) ref_attn_decode_kernel(const T *__
     using G = RaGeom<T, DH>;
     constexpr int V = G::V, COLS = G::COLS, VPR = G::VPR;
     constexpr bool kExact = sizeof(T) == 2;
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ float s_red[kRaThreads / 32];
     __shared__ float s_sum;
     cg::cluster_group cluster = cg::this_cluster();
