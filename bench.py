@@ -412,8 +412,8 @@ def run_b200(args):
         "clocks": clk.summary(),
         # per step: embedding, 28 x (qkv gemv [rms, rope, kv append fused], attention,
         # o gemv [+residual], gate/up gemv [rms, swiglu fused], down gemv [+residual]), lm_head gemv
-        # [final rms fused], argmax [+ sequence lengths advanced]
-        "gpu_launches": K * (1 + 28 * 5 + 2),
+        # [final rms, greedy argmax and sequence lengths advanced, fused]
+        "gpu_launches": K * (1 + 28 * 5 + 1),
     })
     # the long sweep first; the batched and REFERENCE results close the line
     # (a reader of its last characters sees them)
