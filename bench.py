@@ -43,6 +43,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (Qwen2-1.5B arch bf16, bs1 & bs64) + per-op HBM GB/s vs peak"
+SPEC_HBM_GBS = 8000.0  # B200 HBM3e specification (the measured copy peak is in MEASURED_PEAKS.json)
 UNIT = "tok/s"
 
 
@@ -277,7 +278,7 @@ def op_sweep(peak, quick=False):
     def record(op, dtype, shape, nbytes, t):
         gbs = nbytes / t / 1e9
         out.append({"op": op, "dtype": dtype, "shape": shape, "bytes": nbytes, "us": round(t * 1e6, 2),
-                    "gbs": round(gbs, 1), "frac": round(gbs / peak, 3)})
+                    "gbs": round(gbs, 1), "frac": round(gbs / peak, 3), "frac_spec": round(gbs / SPEC_HBM_GBS, 3)})
 
     flat = [1 << 20, 1 << 24, 1 << 28] + ([] if quick else [1 << 30])
     with numerics("fast"):
@@ -318,8 +319,40 @@ def op_sweep(peak, quick=False):
                 del v
     torch.cuda.empty_cache()
     big = [r for r in out if r["bytes"] >= (64 << 20)]
-    return {"unit": "GB/s", "peak": peak, "cases": out,
-            "min_frac_at_64MB_or_more": round(min(r["frac"] for r in big), 3) if big else None}
+    return {"unit": "GB/s", "peak": peak, "spec_peak": SPEC_HBM_GBS, "cases": out,
+            "min_frac_at_64MB_or_more": round(min(r["frac"] for r in big), 3) if big else None,
+            "min_frac_spec_at_64MB_or_more": round(min(r["frac_spec"] for r in big), 3) if big else None}
+
+
+def op_probe(op: str, reps: int = 3):
+    """A few launches of one swept op at a size of 64 MB or more (bf16), for
+    an ncu capture of its DRAM bytes: add and swiglu on 2^25 elements,
+    rms_norm on [43690, 1536], argmax over [256, 151936]."""
+    import torch
+    from wginfer_b200 import numerics, ops
+    g = torch.Generator(device="cuda").manual_seed(5)
+    bf = torch.bfloat16
+    with numerics("fast"):
+        if op in ("add", "swiglu"):
+            n = 1 << 25
+            a, b = torch.randn(n, device="cuda", generator=g).to(bf), torch.randn(n, device="cuda", generator=g).to(bf)
+            c = torch.empty_like(a)
+            fn = (lambda: ops.add(c, a, b)) if op == "add" else (
+                lambda: ops.swiglu(c.view(1, -1), a.view(1, -1), b.view(1, -1)))
+        elif op == "rms_norm":
+            x = torch.randn(43690, 1536, device="cuda", generator=g).to(bf)
+            w = (torch.randn(1536, device="cuda", generator=g) * 0.1 + 1).to(bf)
+            y = torch.empty_like(x)
+            fn = lambda: ops.rms_norm(y, x, w, 1e-6)
+        else:
+            v = torch.randn(256, 151936, device="cuda", generator=g).to(bf)
+            idx = torch.empty(256, dtype=torch.int64, device="cuda")
+            val = torch.empty(256, dtype=bf, device="cuda")
+            fn = lambda: ops.argmax_rows(idx, val, v)
+        for _ in range(reps):
+            fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"op_probe": op, "launches": reps}))
 
 
 def decode_config(args, world):
@@ -559,6 +592,8 @@ def main():
     ap.add_argument("--only-bs64", action="store_true",
                     help="print only the batched-decode result (64 sequences x 2048-token prompts)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op-probe", choices=["add", "swiglu", "rms_norm", "argmax"], default=None,
+                    help="only launch one swept op a few times at >= 64 MB (for an ncu capture)")
     ap.add_argument("--no-reference-numerics", action="store_true",
                     help="skip the REFERENCE-numerics (token-identical) decode measurement")
     ap.add_argument("--no-sweep", action="store_true", help="skip the elementwise/reduction bandwidth sweep")
@@ -567,7 +602,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.op_probe:
+        op_probe(args.op_probe)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.only_bs64:
         world, rank, local = dist_setup(args.gpus)
