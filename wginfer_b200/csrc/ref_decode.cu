@@ -526,10 +526,10 @@ template <typename T, int DH> struct RaGeom {
 };
 
 // scores / probabilities [maxlen rounded up to 4] f32, the V column slice
-// [maxlen][dh / 8], q [dh] f32
+// [maxlen][dh / 8]
 __host__ __device__ inline int ra_scores_len(int maxlen) { return (maxlen + 3) & ~3; }
 size_t ra_smem_bytes(size_t es, int dh, int maxlen) {
-    return (size_t)ra_scores_len(maxlen) * 4 + (size_t)maxlen * (dh / kRaCluster) * es + (size_t)dh * 4;
+    return (size_t)ra_scores_len(maxlen) * 4 + (size_t)maxlen * (dh / kRaCluster) * es;
 }
 
 template <typename T, int DH>
@@ -539,7 +539,6 @@ __global__ void __launch_bounds__(kRaThreads) ref_attn_decode_kernel(const T *__
                                                                      int nkvh, int maxlen, float scale) {
     using G = RaGeom<T, DH>;
     constexpr int V = G::V, COLS = G::COLS, VPR = G::VPR;
-    constexpr bool kExact = sizeof(T) == 2;
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ float s_red[kRaThreads / 32];
     __shared__ float s_sum;
@@ -550,7 +549,6 @@ __global__ void __launch_bounds__(kRaThreads) ref_attn_decode_kernel(const T *__
     const int tid = threadIdx.x;
     float *sc = reinterpret_cast<float *>(smem);                       // [maxlen]
     T *vs = reinterpret_cast<T *>(sc + ra_scores_len(maxlen));         // [maxlen][COLS]
-    float *qf = reinterpret_cast<float *>(vs + (size_t)maxlen * COLS);  // [DH]
 
     pdl_trigger();
     pdl_wait();  // q and the newest K/V row come from the previous kernel
@@ -567,35 +565,33 @@ __global__ void __launch_bounds__(kRaThreads) ref_attn_decode_kernel(const T *__
         __pipeline_memcpy_async(vs + (size_t)j * COLS + c * V, vb + (size_t)j * rstride + c * V, 16);
     }
     __pipeline_commit();
-    for (int c = tid; c < DH; c += kRaThreads) qf[c] = ldf(q, ((size_t)b * nh + h) * DH + c);
-    __syncthreads();
 
     // scores (self_attention_cpu.cpp:37-45): scale * (sequential dot over d);
     // this CTA's keys are [j0, j1), one key per thread per pass, two passes
-    // interleaved; each score goes to CTA 0
+    // interleaved; each score goes to CTA 0. The key rows and the query are
+    // loaded together (one round trip; plain coherent loads, both were
+    // written by the previous kernel), the query kept as 16-byte vectors of
+    // T for the chain steps.
     float *sc0 = cluster.map_shared_rank(sc, 0);
     const int per = (L + kRaCluster - 1) / kRaCluster;
     const int j0 = r * per, j1 = min(L, j0 + per);
+    const uint4 *qrow = reinterpret_cast<const uint4 *>(q + ((size_t)b * nh + h) * DH);
     for (int ja = j0 + tid; ja < j1; ja += 2 * kRaThreads) {
         const int jb = ja + kRaThreads;
         const bool hb = jb < j1;
-        // plain (coherent) loads: the newest row was written by the previous kernel
-        Vec16<T> ka[VPR], kbv[VPR];
+        uint4 ka[VPR], kbv[VPR], qv[VPR];
 #pragma unroll
         for (int u = 0; u < VPR; u++) {
-            ka[u].u = *reinterpret_cast<const uint4 *>(kb + (size_t)ja * rstride + u * V);
-            kbv[u].u = hb ? *reinterpret_cast<const uint4 *>(kb + (size_t)jb * rstride + u * V)
-                          : make_uint4(0u, 0u, 0u, 0u);
+            ka[u] = *reinterpret_cast<const uint4 *>(kb + (size_t)ja * rstride + u * V);
+            kbv[u] = hb ? *reinterpret_cast<const uint4 *>(kb + (size_t)jb * rstride + u * V)
+                        : make_uint4(0u, 0u, 0u, 0u);
+            qv[u] = qrow[u];
         }
         float aa = 0.f, ab = 0.f;
 #pragma unroll
         for (int u = 0; u < VPR; u++) {
-#pragma unroll
-            for (int e = 0; e < V; e++) {
-                const float qv = qf[u * V + e];
-                aa = chain_step<kExact>(aa, qv, Elem<T>::load(ka[u].e[e]));
-                ab = chain_step<kExact>(ab, qv, Elem<T>::load(kbv[u].e[e]));
-            }
+            chain_vec<T>(aa, qv[u], ka[u]);
+            chain_vec<T>(ab, qv[u], kbv[u]);
         }
         sc0[ja] = __fmul_rn(scale, aa);
         if (hb) sc0[jb] = __fmul_rn(scale, ab);
@@ -649,11 +645,16 @@ __global__ void __launch_bounds__(kRaThreads) ref_attn_decode_kernel(const T *__
     if (tid < COLS) {
         float acc = 0.f;
         int j = 0;
+        const uint32_t sc_s = smem_u32(sc);
         for (; j + 16 <= L; j += 16) {  // 16 keys' operands loaded, then 16 chain steps
             float4 p4[4];
             float vv[16];
 #pragma unroll
-            for (int q = 0; q < 4; q++) p4[q] = *reinterpret_cast<const float4 *>(sc + j + 4 * q);
+            for (int q = 0; q < 4; q++) {
+                const uint4 w = lds128(sc_s + (uint32_t)((j + 4 * q) * 4));
+                p4[q] = make_float4(__uint_as_float(w.x), __uint_as_float(w.y), __uint_as_float(w.z),
+                                    __uint_as_float(w.w));
+            }
 #pragma unroll
             for (int u = 0; u < 16; u++) vv[u] = Elem<T>::load(vs[(size_t)(j + u) * COLS + tid]);
 #pragma unroll
