@@ -211,11 +211,12 @@ def _bf16_bits_of_f32(a):
 
 
 @pytest.mark.parametrize("mode", ["fast", "reference"])
-@pytest.mark.parametrize("B", [1, 3])
+@pytest.mark.parametrize("B", [1, 3, 20])
 def test_decode_step_fused_argmax_ties_and_nan(oracle, cuda, mode, B):
     """The decode step's greedy token comes out of the lm_head launch itself
     (a (value, first index) key folded across CTAs, model.cpp:398-407 /
-    argmax_cpu.cpp:26-47). Each step's tokens must equal the oracle's
+    argmax_cpu.cpp:26-47; 20 rows take the tensor-core GEMM's argmax
+    epilogue in FAST numerics, two input tiles x 8 weight tiles of CTAs). Each step's tokens must equal the oracle's
     sequential argmax of the logits that same launch wrote: with lm_head rows
     repeating every 7 rows (every maximum is tied 143 times), with NaN logits
     at index 0 (the scan keeps them) and elsewhere (never chosen)."""

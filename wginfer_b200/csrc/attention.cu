@@ -25,6 +25,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -760,38 +761,75 @@ int launch_mma_attn(T *out, const T *q, KvDense<T> src, const AttnShape &sh, cud
     return check_launch("self_attention(mma)");
 }
 
-// ---- FAST batched decode: GQA groups on the tensor cores --------------------
+// ---- FAST batched decode: GQA groups on the tensor cores, K/V by TMA --------
 // One CTA = one (sequence, kv head) and one slice of its keys. The hpc query
 // heads that share the kv head are the 16 rows of an m16n8k16 A tile (rows
 // past hpc are zero), so every K/V row is read once per kv head and feeds
-// hpc query heads through mma.sync. Four warps split the CTA's keys; each
-// streams its own 16-key K/V tiles through a double-buffered shared-memory
-// stage (cp.async), keeps a running max/sum per row and O += P V in
-// registers. The warps fold in shared memory, then the CTAs of the cluster
-// (the key slices) fold in CTA 0 through distributed shared memory.
+// hpc query heads through mma.sync. A producer warp streams the slice in
+// stages of kDStage keys: one TMA box of K and one of V per stage (the kv
+// head's DH columns as DH/64 blocks of 128 bytes, 128-byte swizzle; 16 KB
+// per box at DH = 128) into a ring of kDS stages on full/empty mbarriers.
+// Four consumer warps take 16 keys of each stage, keep a running max/sum per
+// row and O += P V in registers. Few large boxes keep about 200 KB in flight
+// per SM (two CTAs), enough to stream at HBM rate; per-warp cp.async tiles of
+// 16 keys left the kernel waiting on its loads at 0.47 of HBM. After the key
+// loop the ring holds the warps' partial rows, the warps fold in shared
+// memory, then the CTAs of the cluster (the key slices) fold in CTA 0 through
+// distributed shared memory.
 // Roofline: HBM, 2 * B * L * nkvh * d * size bytes of K/V.
-constexpr int kDW = 4;        // warps per CTA
-constexpr int kDK = 16;       // keys per warp tile (small enough for two CTAs per SM)
-constexpr int kDN = kDK / 8;  // n-tiles of 8 keys per warp tile
+constexpr int kDW = 4;                     // consumer warps per CTA
+constexpr int kDThreads = (kDW + 1) * 32;  // and the producer warp
+constexpr int kDK = 16;                    // keys per consumer warp and stage
+constexpr int kDN = kDK / 8;               // n-tiles of 8 keys
+constexpr int kDStage = kDW * kDK;         // keys per stage
+constexpr int kDS = 3;                     // ring stages
+constexpr long long kDWaitCycles = 2000000000ll;  // ~1 s: a wait that long records an error
 
 template <typename T, int DH> struct MmaDecLayout {
-    static constexpr int RS = DH + 8;
-    static constexpr size_t tile = (size_t)kDK * RS * sizeof(T);      // one K or V tile
-    static constexpr size_t warp_stage = 4 * tile;                    // K, V x 2 buffers
-    static constexpr size_t qs = 0;                                   // [16][RS] T
-    static constexpr size_t kv = ((size_t)16 * RS * sizeof(T) + 127) & ~(size_t)127;
-    static constexpr size_t xo = kv + kDW * warp_stage;               // rank 0: [ns][hpc][DH] f32
-    static constexpr size_t bytes(int ns, int hpc) { return xo + (size_t)ns * hpc * DH * 4; }
+    static constexpr int RS = DH + 8;                                // Q tile row stride (elements)
+    static constexpr size_t box = (size_t)kDStage * DH * sizeof(T);  // one K or V box
+    static constexpr size_t stage = 2 * box;
+    static constexpr size_t qs = kDS * stage;  // [16][RS] T after the ring (ring at 0, 1024-aligned)
+    // + 1 KB: the ring starts at the first 1024-byte boundary of dynamic
+    // shared memory (TMA boxes with 128-byte swizzle)
+    static constexpr size_t bytes = qs + (size_t)16 * RS * sizeof(T) + 1024;
+    // reused from the ring after the key loop: each consumer warp's
+    // unnormalised [16][DH] f32 rows, then (CTA 0) the slices' [ns][hpc][DH]
+    static constexpr size_t xo = (size_t)kDW * 16 * DH * 4;
+    static_assert(xo + (size_t)kMaxCluster * 16 * DH * 4 <= qs, "the fold areas must fit in the ring");
 };
 
+// Byte offset of 16-byte chunk ch (of DH / 8) of box row r: the box is DH / 64
+// blocks of [kDStage rows][128 bytes], chunk c of row r stored at c ^ (r % 8).
+__device__ __forceinline__ uint32_t dec_swz(int r, int ch) {
+    return (uint32_t)((ch >> 3) * (kDStage * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
+}
+__device__ __forceinline__ void ldsm4a(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm4a_t(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
 template <typename T, int DH>
-__global__ void __launch_bounds__(kDW * 32) attn_mma_decode_kernel(const T *__restrict__ q, KvCache<T> src,
-                                                                   T *__restrict__ out, AttnShape sh) {
+__global__ void __launch_bounds__(kDThreads) attn_mma_decode_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                                    const __grid_constant__ CUtensorMap tmV,
+                                                                    const T *__restrict__ q, KvCache<T> src,
+                                                                    T *__restrict__ out, AttnShape sh,
+                                                                    int rows_per_seq, unsigned long long *err) {
     using Lay = MmaDecLayout<T, DH>;
     constexpr int RS = Lay::RS, CPR = DH / 8, NKS = DH / 16, NDT = DH / 8;
-    extern __shared__ __align__(128) unsigned char smem[];
+    // the dynamic shared memory symbol is shared with this file's other
+    // kernels (16-byte alignment): the ring's 1024-byte boundary is found at
+    // run time, the same offset in every CTA of the cluster
+    extern __shared__ __align__(16) unsigned char smem_raw_dec[];
+    unsigned char *smem = smem_raw_dec + ((1024u - (smem_u32(smem_raw_dec) & 1023u)) & 1023u);
     T *qs = reinterpret_cast<T *>(smem + Lay::qs);
-    float *xo = reinterpret_cast<float *>(smem + Lay::xo);
+    __shared__ __align__(8) uint64_t full[kDS], empty[kDS];
     __shared__ float wm[kDW][16], wl[kDW][16];
     __shared__ float xm[kMaxCluster][16], xl[kMaxCluster][16];
     cg::cluster_group cluster = cg::this_cluster();
@@ -802,155 +840,187 @@ __global__ void __launch_bounds__(kDW * 32) attn_mma_decode_kernel(const T *__re
     const T *k, *v;
     int nkeys, nvis;
     bool uniform;
-    src.row(sh, b, k, v, nkeys, nvis, uniform);
-    const size_t kst = (size_t)sh.nkvh * DH;
-    const T *kb = k + (size_t)kvh * DH, *vb = v + (size_t)kvh * DH;
+    src.row(sh, b, k, v, nkeys, nvis, uniform);  // lengths were set by an earlier step
     const int per = (nvis + ns - 1) / ns;
     const int c0 = min(rank * per, nvis), c1 = min(c0 + per, nvis);
-    const int wper = (c1 - c0 + kDW - 1) / kDW;
-    const int w0 = min(c0 + warp * wper, c1), w1 = min(w0 + wper, c1);
-    const int ntiles = (w1 - w0 + kDK - 1) / kDK;
-    T *kbuf = reinterpret_cast<T *>(smem + Lay::kv + (size_t)warp * Lay::warp_stage);  // [2][kDK][RS]
-    T *vbuf = kbuf + 2 * kDK * RS;                                                     // [2][kDK][RS]
-    auto load_tile = [&](int t) {  // this warp's tile t
-        if (t < ntiles) {
-            T *kd = kbuf + (t & 1) * kDK * RS, *vd = vbuf + (t & 1) * kDK * RS;
-            for (int c = lane; c < kDK * CPR; c += 32) {
-                const int r = c / CPR, cc = c - r * CPR, j = w0 + t * kDK + r;
-                if (j < w1) {
-                    __pipeline_memcpy_async(kd + r * RS + cc * 8, kb + (size_t)j * kst + cc * 8, 16);
-                    __pipeline_memcpy_async(vd + r * RS + cc * 8, vb + (size_t)j * kst + cc * 8, 16);
-                } else {
-                    *reinterpret_cast<uint4 *>(kd + r * RS + cc * 8) = make_uint4(0, 0, 0, 0);
-                    *reinterpret_cast<uint4 *>(vd + r * RS + cc * 8) = make_uint4(0, 0, 0, 0);
-                }
-            }
+    const int nst = (c1 - c0 + kDStage - 1) / kDStage;  // stages of this slice
+    if (tid == 0) {
+        for (int s = 0; s < kDS; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kDW);
         }
-        __pipeline_commit();
-    };
-    pdl_trigger();
-    pdl_wait();  // q and the newest cache rows come from the previous kernel
-    for (int c = tid; c < 16 * CPR; c += kDW * 32) {
-        const int r = c / CPR, cc = c - r * CPR;
-        T *dst = qs + r * RS + cc * 8;
-        if (r < hpc) __pipeline_memcpy_async(dst, q + ((size_t)b * sh.nh + h0 + r) * DH + cc * 8, 16);
-        else *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+        mbar_init_fence();
     }
-    __pipeline_commit();
-    load_tile(0);
-    load_tile(1);
-    __pipeline_wait_prior(2);
-    __syncthreads();  // the Q tile is shared by the four warps
-    uint32_t qf[NKS][4];
-#pragma unroll
-    for (int kk = 0; kk < NKS; kk++)
-        ldsm4(qf[kk], qs + ((lane & 7) + ((lane >> 3) & 1) * 8) * RS + kk * 16 + (lane >> 4) * 8);
+    __syncthreads();
+    pdl_trigger();
     const float sc2 = sh.scale * 1.4426950408889634f;
     float o[NDT][4];
 #pragma unroll
     for (int i = 0; i < NDT; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
 
-    for (int t = 0; t < ntiles; t++) {
-        __pipeline_wait_prior(1);
-        __syncwarp();
-        const T *kt = kbuf + (t & 1) * kDK * RS, *vt = vbuf + (t & 1) * kDK * RS;
-        float s[kDN][4];
-#pragma unroll
-        for (int n = 0; n < kDN; n++) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < NKS; kk++) {
-#pragma unroll
-            for (int n = 0; n < kDN; n += 2) {
-                uint32_t bb[4];
-                ldsm4(bb, kt + (n * 8 + (lane & 7) + (lane >> 4) * 8) * RS + kk * 16 + ((lane >> 3) & 1) * 8);
-                mma16816<T>(s[n], qf[kk], bb[0], bb[1]);
-                mma16816<T>(s[n + 1], qf[kk], bb[2], bb[3]);
+    if (warp == kDW) {
+        // producer: stage t holds keys [c0 + t kDStage, c0 + (t + 1) kDStage);
+        // rows past c1 are masked (K) or cleared (V) by the consumers. Rows
+        // before the newest one were written by earlier steps, so they are
+        // requested before the wait for the previous kernel.
+        if (lane == 0) {
+            const int row0 = b * rows_per_seq + c0, blk = kvh * (DH / 64);
+            bool waited = false;
+            for (int t = 0; t < nst; t++) {
+                const int s = t % kDS;
+                if (t >= kDS && !mbar_wait(&empty[s], ((t / kDS) - 1) & 1, kDWaitCycles)) {
+                    record_device_error(err, 9, (long long)blockIdx.y);
+                    break;
+                }
+                if (!waited && c0 + (t + 1) * kDStage >= nvis) {
+                    pdl_wait();  // this stage holds the newest row
+                    waited = true;
+                }
+                unsigned char *st = smem + (size_t)s * Lay::stage;
+                mbar_arrive_expect_tx(&full[s], (unsigned)Lay::stage);
+                tma_load_box3(st, &tmK, 0, row0 + t * kDStage, blk, &full[s]);
+                tma_load_box3(st + Lay::box, &tmV, 0, row0 + t * kDStage, blk, &full[s]);
             }
         }
-        float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-        for (int n = 0; n < kDN; n++) {
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const int j = w0 + t * kDK + n * 8 + 2 * t4 + (c & 1);
-                const float val = j < w1 ? (uniform ? 0.f : s[n][c] * sc2) : -INFINITY;
-                s[n][c] = val;
-                mx[c >> 1] = fmaxf(mx[c >> 1], val);
-            }
+    } else {
+        pdl_wait();  // q comes from the previous kernel
+        for (int c = tid; c < 16 * CPR; c += kDW * 32) {
+            const int r = c / CPR, cc = c - r * CPR;
+            T *dst = qs + r * RS + cc * 8;
+            if (r < hpc) __pipeline_memcpy_async(dst, q + ((size_t)b * sh.nh + h0 + r) * DH + cc * 8, 16);
+            else *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
         }
-        float corr[2];
+        __pipeline_commit();
+        __pipeline_wait_prior(0);
+        asm volatile("bar.sync 1, %0;" ::"r"(kDW * 32) : "memory");  // the Q tile is shared by the consumers
+        uint32_t qf[NKS][4];
+#pragma unroll
+        for (int kk = 0; kk < NKS; kk++)
+            ldsm4(qf[kk], qs + ((lane & 7) + ((lane >> 3) & 1) * 8) * RS + kk * 16 + (lane >> 4) * 8);
+        bool bad = false;
+        const int wr = warp * kDK;  // this warp's first row of each stage
+        for (int t = 0; t < nst; t++) {
+            const int s = t % kDS;
+            if (!bad && !mbar_wait(&full[s], (t / kDS) & 1, kDWaitCycles)) {
+                if (lane == 0) record_device_error(err, 9, (long long)blockIdx.y);
+                bad = true;
+            }
+            const int j0 = c0 + t * kDStage + wr;  // key of this warp's first row
+            const uint32_t kt = smem_u32(smem + (size_t)s * Lay::stage), vt = kt + (uint32_t)Lay::box;
+            if (!bad && j0 < c1) {
+                if (j0 + kDK > c1) {
+                    // rows past the slice hold other positions (or fill):
+                    // their V rows are cleared so that P = 0 meets finite values
+                    for (int e = lane; e < kDK * CPR; e += 32) {
+                        const int r = e / CPR, ch = e - r * CPR;
+                        if (j0 + r >= c1) {
+                            const uint32_t a = vt + dec_swz(wr + r, ch);
+                            asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
+                        }
+                    }
+                    // written through the generic proxy: ordered before the
+                    // next TMA into this stage
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                }
+                float sacc[kDN][4];
+#pragma unroll
+                for (int n = 0; n < kDN; n++) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
+#pragma unroll
+                for (int kk = 0; kk < NKS; kk++) {
+#pragma unroll
+                    for (int n = 0; n < kDN; n += 2) {
+                        uint32_t bb[4];
+                        ldsm4a(bb, kt + dec_swz(wr + n * 8 + (lane & 7) + (lane >> 4) * 8, kk * 2 + ((lane >> 3) & 1)));
+                        mma16816<T>(sacc[n], qf[kk], bb[0], bb[1]);
+                        mma16816<T>(sacc[n + 1], qf[kk], bb[2], bb[3]);
+                    }
+                }
+                float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+                for (int n = 0; n < kDN; n++) {
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const int j = j0 + n * 8 + 2 * t4 + (c & 1);
+                        const float val = j < c1 ? sacc[n][c] * sc2 : -INFINITY;
+                        sacc[n][c] = val;
+                        mx[c >> 1] = fmaxf(mx[c >> 1], val);
+                    }
+                }
+                float corr[2];
+#pragma unroll
+                for (int r = 0; r < 2; r++) {
+                    mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+                    mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+                    const float mnew = fmaxf(mrow[r], mx[r]);
+                    corr[r] = mnew == -INFINITY ? 1.f : ex2(mrow[r] - mnew);
+                    mrow[r] = mnew;
+                    lrow[r] *= corr[r];
+                }
+#pragma unroll
+                for (int i = 0; i < NDT; i++) {
+                    o[i][0] *= corr[0];
+                    o[i][1] *= corr[0];
+                    o[i][2] *= corr[1];
+                    o[i][3] *= corr[1];
+                }
+#pragma unroll
+                for (int n = 0; n < kDN; n++) {
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const float m = mrow[c >> 1];
+                        const float p = m == -INFINITY ? 0.f : ex2(sacc[n][c] - m);
+                        sacc[n][c] = p;
+                        lrow[c >> 1] += p;
+                    }
+                }
+                uint32_t pa[4];
+                pa[0] = pack2<T>(sacc[0][0], sacc[0][1]);
+                pa[1] = pack2<T>(sacc[0][2], sacc[0][3]);
+                pa[2] = pack2<T>(sacc[1][0], sacc[1][1]);
+                pa[3] = pack2<T>(sacc[1][2], sacc[1][3]);
+#pragma unroll
+                for (int nd = 0; nd < NDT; nd += 2) {
+                    uint32_t bb[4];
+                    ldsm4a_t(bb, vt + dec_swz(wr + (lane & 7) + ((lane >> 3) & 1) * 8, nd + (lane >> 4)));
+                    mma16816<T>(o[nd], pa, bb[0], bb[1]);
+                    mma16816<T>(o[nd + 1], pa, bb[2], bb[3]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
 #pragma unroll
         for (int r = 0; r < 2; r++) {
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-            const float mnew = fmaxf(mrow[r], mx[r]);
-            corr[r] = mnew == -INFINITY ? 1.f : ex2(mrow[r] - mnew);
-            mrow[r] = mnew;
-            lrow[r] *= corr[r];
+            lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+            lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
         }
-#pragma unroll
-        for (int i = 0; i < NDT; i++) {
-            o[i][0] *= corr[0];
-            o[i][1] *= corr[0];
-            o[i][2] *= corr[1];
-            o[i][3] *= corr[1];
+        if (t4 == 0) {
+            wm[warp][g] = mrow[0];
+            wm[warp][g + 8] = mrow[1];
+            wl[warp][g] = lrow[0];
+            wl[warp][g + 8] = lrow[1];
         }
+        // every consumer is past its last stage (and so every box has landed):
+        // this warp's unnormalised rows, [16][DH] f32, go into the ring
+        asm volatile("bar.sync 1, %0;" ::"r"(kDW * 32) : "memory");
+        float *ow = reinterpret_cast<float *>(smem) + (size_t)warp * 16 * DH;
 #pragma unroll
-        for (int n = 0; n < kDN; n++) {
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const float m = mrow[c >> 1];
-                const float p = m == -INFINITY ? 0.f : ex2(s[n][c] - m);
-                s[n][c] = p;
-                lrow[c >> 1] += p;
-            }
+        for (int nd = 0; nd < NDT; nd++) {
+            const int col = nd * 8 + 2 * t4;
+            ow[g * DH + col] = o[nd][0];
+            ow[g * DH + col + 1] = o[nd][1];
+            ow[(g + 8) * DH + col] = o[nd][2];
+            ow[(g + 8) * DH + col + 1] = o[nd][3];
         }
-#pragma unroll
-        for (int kk = 0; kk < kDK / 16; kk++) {
-            uint32_t pa[4];
-            pa[0] = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
-            pa[1] = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
-            pa[2] = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-            pa[3] = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-#pragma unroll
-            for (int nd = 0; nd < NDT; nd += 2) {
-                uint32_t bb[4];
-                ldsm4_t(bb, vt + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * RS + nd * 8 + (lane >> 4) * 8);
-                mma16816<T>(o[nd], pa, bb[0], bb[1]);
-                mma16816<T>(o[nd + 1], pa, bb[2], bb[3]);
-            }
-        }
-        __syncwarp();  // this buffer is refilled next
-        load_tile(t + 2);
-    }
-    __pipeline_wait_prior(0);
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-        lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
-        lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
-    }
-    if (t4 == 0) {
-        wm[warp][g] = mrow[0];
-        wm[warp][g + 8] = mrow[1];
-        wl[warp][g] = lrow[0];
-        wl[warp][g + 8] = lrow[1];
-    }
-    // this warp's unnormalised rows, [16][DH] f32, into its idle stage
-    float *ow = reinterpret_cast<float *>(kbuf);
-#pragma unroll
-    for (int nd = 0; nd < NDT; nd++) {
-        const int col = nd * 8 + 2 * t4;
-        ow[g * DH + col] = o[nd][0];
-        ow[g * DH + col + 1] = o[nd][1];
-        ow[(g + 8) * DH + col] = o[nd][2];
-        ow[(g + 8) * DH + col + 1] = o[nd][3];
     }
     __syncthreads();
+    cluster.sync();  // every CTA is past its key loop: CTA 0's ring may take the slices' rows
     // fold the warps into this CTA's slice and push it to CTA 0 of the cluster
-    float *xo0 = cluster.map_shared_rank(xo, 0);
+    float *xo0 = cluster.map_shared_rank(reinterpret_cast<float *>(smem + Lay::xo), 0);
     float *xm0 = cluster.map_shared_rank(&xm[0][0], 0), *xl0 = cluster.map_shared_rank(&xl[0][0], 0);
-    for (int x = tid; x < hpc * DH; x += kDW * 32) {
+    for (int x = tid; x < hpc * DH; x += kDThreads) {
         const int row = x / DH, col = x - row * DH;
         float M = -INFINITY;
 #pragma unroll
@@ -962,7 +1032,7 @@ __global__ void __launch_bounds__(kDW * 32) attn_mma_decode_kernel(const T *__re
                 if (wl[w][row] > 0.f) {
                     const float e = ex2(wm[w][row] - M);
                     L += wl[w][row] * e;
-                    O += reinterpret_cast<const float *>(smem + Lay::kv + (size_t)w * Lay::warp_stage)[row * DH + col] * e;
+                    O += reinterpret_cast<const float *>(smem)[((size_t)w * 16 + row) * DH + col] * e;
                 }
             }
         }
@@ -974,7 +1044,8 @@ __global__ void __launch_bounds__(kDW * 32) attn_mma_decode_kernel(const T *__re
     }
     cluster.sync();
     if (rank == 0) {
-        for (int x = tid; x < hpc * DH; x += kDW * 32) {
+        const float *xo = reinterpret_cast<const float *>(smem + Lay::xo);
+        for (int x = tid; x < hpc * DH; x += kDThreads) {
             const int row = x / DH, col = x - row * DH;
             float MM = -INFINITY;
             for (int r = 0; r < ns; r++) MM = fmaxf(MM, xm[r][row]);
@@ -993,18 +1064,44 @@ __global__ void __launch_bounds__(kDW * 32) attn_mma_decode_kernel(const T *__re
     }
 }
 
-template <typename T, int DH>
-int launch_mma_decode(T *out, const T *q, KvCache<T> src, const AttnShape &sh, cudaStream_t s) {
-    // key slices: about 512 keys per CTA at the longest length this launch
-    // serves (the cluster size depends only on it, so a captured graph stays
-    // valid as the caches grow)
-    int ns = (sh.L + 511) / 512;
+// Slices per (sequence, kv head): as many as keep every CTA of the launch
+// resident at once (two per SM), at least 128 keys per slice, at most a
+// portable cluster. One wave of long slices beats several waves of short
+// ones: at 64 sequences x 2 kv heads x 2300 keys, 2 slices (256 CTAs) ran
+// the step's attention in 36 us serialised, 5 slices (640 CTAs) in 45 us,
+// 8 in 53 us. Depends only on the batch and the cache capacity, so a captured
+// graph stays valid as the caches grow.
+inline int mma_decode_slices(const AttnShape &sh) {
+    const long pairs = (long)sh.S * sh.nkvh;
+    long ns = 2L * sm_count() / (pairs > 0 ? pairs : 1);
+    const long by_len = sh.L / 128;
+    if (ns > by_len) ns = by_len;
     if (ns > kMaxCluster) ns = kMaxCluster;
     if (ns < 1) ns = 1;
+    return (int)ns;
+}
+
+// The TMA view of a cache: [B * rows_per_seq rows][nkvh * d columns]; false
+// when the caches do not have that shape or the driver refuses the maps.
+template <typename T>
+bool mma_decode_maps(CUtensorMap *tk, CUtensorMap *tv, const KvCache<T> &src, const AttnShape &sh, int &rows_per_seq) {
+    const size_t w = (size_t)sh.nkvh * sh.d;
+    if (src.seq_stride % w || !aligned16(src.k) || !aligned16(src.v)) return false;
+    const size_t rps = src.seq_stride / w, rows = (size_t)sh.S * rps;
+    if (rps < (size_t)sh.L || rows >= (1ull << 31) || w >= (1ull << 31)) return false;
+    rows_per_seq = (int)rps;
+    return tma_map_row_stages(tk, src.k, (int)sizeof(T), (int)rows, (int)w, kDStage, sh.d / 64) &&
+           tma_map_row_stages(tv, src.v, (int)sizeof(T), (int)rows, (int)w, kDStage, sh.d / 64);
+}
+
+template <typename T, int DH>
+int launch_mma_decode(T *out, const T *q, KvCache<T> src, const AttnShape &sh, const CUtensorMap &tk,
+                      const CUtensorMap &tv, int rows_per_seq, cudaStream_t s) {
+    const int ns = mma_decode_slices(sh);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ns, (unsigned)(sh.S * sh.nkvh), 1);
-    cfg.blockDim = dim3(kDW * 32, 1, 1);
-    cfg.dynamicSmemBytes = MmaDecLayout<T, DH>::bytes(ns, sh.nh / sh.nkvh);
+    cfg.blockDim = dim3(kDThreads, 1, 1);
+    cfg.dynamicSmemBytes = MmaDecLayout<T, DH>::bytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1015,7 +1112,8 @@ int launch_mma_decode(T *out, const T *q, KvCache<T> src, const AttnShape &sh, c
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_mma_decode_kernel<T, DH>, q, src, out, sh);
+    cudaError_t e =
+        cudaLaunchKernelEx(&cfg, attn_mma_decode_kernel<T, DH>, tk, tv, q, src, out, sh, rows_per_seq, dev_error_ptr());
     if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "self_attention(mma decode): %s", cudaGetErrorString(e));
     return check_launch("self_attention(mma decode)");
 }
@@ -1169,9 +1267,9 @@ template <typename T, class Src> void set_attrs() {
     cudaFuncSetAttribute(attn_fast_kernel<T, Src, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if constexpr (sizeof(T) == 2 && IsKvCache<Src>::value) {
         cudaFuncSetAttribute(attn_mma_decode_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)MmaDecLayout<T, 128>::bytes(kMaxCluster, 16));
+                             (int)MmaDecLayout<T, 128>::bytes);
         cudaFuncSetAttribute(attn_mma_decode_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)MmaDecLayout<T, 64>::bytes(kMaxCluster, 16));
+                             (int)MmaDecLayout<T, 64>::bytes);
     }
     if constexpr (sizeof(T) == 2) {
         cudaFuncSetAttribute(attn_mma_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1220,9 +1318,12 @@ int launch_attn(T *out, const T *q, Src src, const AttnShape &sh, bool ref, void
     if constexpr (sizeof(T) == 2 && IsKvCache<Src>::value) {
         // batched decode: one CTA per (sequence, kv head) and key slice, the
         // query heads of the group as the rows of a tensor-core tile
-        if (vec && sh.d == sh.dv && (sh.d == 128 || sh.d == 64) && sh.nh / sh.nkvh <= 16 && sh.S * sh.nkvh >= 32)
-            return sh.d == 128 ? launch_mma_decode<T, 128>(out, q, src, sh, s)
-                               : launch_mma_decode<T, 64>(out, q, src, sh, s);
+        CUtensorMap tk, tv;
+        int rps = 0;
+        if (vec && sh.d == sh.dv && (sh.d == 128 || sh.d == 64) && sh.nh / sh.nkvh <= 16 && sh.S * sh.nkvh >= 32 &&
+            mma_decode_maps(&tk, &tv, src, sh, rps))
+            return sh.d == 128 ? launch_mma_decode<T, 128>(out, q, src, sh, tk, tv, rps, s)
+                               : launch_mma_decode<T, 64>(out, q, src, sh, tk, tv, rps, s);
     }
     if (vec && sh.d == sh.dv && (sh.d == 128 || sh.d == 64) && (long)sh.S * sh.nh < 2L * sm_count()) {
         // few query rows: one head per warp-group, no block barriers in the key loop

@@ -20,6 +20,10 @@ __device__ __forceinline__ void mbar_init_fence() {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *b, unsigned bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
 }
+// One plain arrival.
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
 // Waits for the phase of the given parity to complete; polls, and checks the
 // SM cycle counter every 64 polls. false after max_cycles.
 __device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned parity, long long max_cycles) {

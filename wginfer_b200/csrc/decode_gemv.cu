@@ -452,7 +452,7 @@ int dispatch(const DecodeGemvParams &p0, int pro, int epi, cudaStream_t s) {
                 "decode_gemv: K = %d is not a whole number of 16-byte vectors", p0.K);
     // more than 8 rows of bf16: one tensor-core GEMM over all rows (the RMS
     // prologue first materialised into p0.xn)
-    if (std::is_same<T, __nv_bfloat16>::value && p0.M0 > kMaxMT && epi != EPI_ARGMAX && (pro == PRO_PLAIN || p0.xn)) {
+    if (std::is_same<T, __nv_bfloat16>::value && p0.M0 > kMaxMT && (pro == PRO_PLAIN || p0.xn)) {
         DecodeGemvParams p = p0;
         p.M = p0.M0;
         if (pro == PRO_RMS) p.x = p0.xn;
@@ -464,6 +464,8 @@ int dispatch(const DecodeGemvParams &p0, int pro, int epi, cudaStream_t s) {
             return tc_gemm(p, epi, s);
         }
     }
+    WGB_REQUIRE(epi != EPI_ARGMAX || p0.M0 <= kMaxMT, WGB_ERR_UNSUPPORTED,
+                "decode_gemv: argmax epilogue over %d rows needs bf16 and the tensor-core path", p0.M0);
     // chunks of up to 8 input rows; each chunk re-reads the weights
     for (int m0 = 0; m0 < p0.M0; m0 += kMaxMT) {
         DecodeGemvParams p = p0;

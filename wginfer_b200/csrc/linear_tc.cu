@@ -27,6 +27,7 @@
 
 #include <atomic>
 
+#include "argmax_key.cuh"
 #include "common.cuh"
 #include "decode_common.cuh"
 #include "kernels.h"
@@ -42,6 +43,7 @@ constexpr int kTcMaxStages = 8;
 constexpr int kTileW = 128;      // weight rows per CTA (MMA M)
 constexpr int kEpiRows = 32;  // input rows per epilogue chunk
 constexpr size_t kEpiTileBytes = (size_t)kEpiRows * kTileW * 2;  // its bf16 staging tile
+constexpr int kTcArgmaxRows = 256;  // input rows of a fused lm_head + argmax launch
 constexpr long long kTcWaitCycles = 4000000000ll;  // a stage stalled this long (about 2 s) counts as a failure
 
 __device__ __forceinline__ uint32_t s_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -186,7 +188,7 @@ __device__ __forceinline__ void tc_epi_stage(__nv_bfloat16 *S, int row, const fl
 
 template <int EPI>
 __device__ __forceinline__ void tc_epi_emit(const DecodeGemvParams &p, const __nv_bfloat16 *S, int n0, int mc,
-                                            int cols, int et) {
+                                            int cols, int et, unsigned long long *s_key = nullptr) {
     using T = __nv_bfloat16;
     constexpr int kPer = kEpiRows * kTileW / 8 / (kTcEpiWarps * 32);  // 16-byte pieces per thread (4)
     const int nc = (et & 15) * 8;                                        // first weight row of the piece
@@ -194,7 +196,38 @@ __device__ __forceinline__ void tc_epi_emit(const DecodeGemvParams &p, const __n
     Vec16<T> sv[kPer];
 #pragma unroll
     for (int k = 0; k < kPer; k++) sv[k].u = *reinterpret_cast<const uint4 *>(S + (jb + 8 * k) * kTileW + nc);
-    if constexpr (EPI == EPI_STORE) {
+    if constexpr (EPI == EPI_ARGMAX) {
+        // lm_head + greedy argmax: the logits are stored as they are, and each
+        // input row's best (value, first index) key over this thread's 8
+        // weight rows is folded over the 16 threads of the row, then into the
+        // CTA's key for the row (argmax_key.cuh)
+        T *out = reinterpret_cast<T *>(p.out);
+        const bool vec = n0 + nc + 8 <= p.N && (p.ldo & 7) == 0 && ((uintptr_t)out & 15) == 0;
+#pragma unroll
+        for (int k = 0; k < kPer; k++) {
+            const int j = jb + 8 * k, m = mc + j;
+            const bool live = j < cols && m < p.M;
+            unsigned long long key = 0ull;
+            if (live) {
+                const size_t off = (size_t)m * p.ldo + n0 + nc;
+                if (vec) *reinterpret_cast<uint4 *>(out + off) = sv[k].u;
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    if (n0 + nc + e < p.N) {
+                        if (!vec) out[off + e] = sv[k].e[e];
+                        const unsigned long long ke = key_or_zero(Elem<T>::load(sv[k].e[e]), (uint32_t)(n0 + nc + e));
+                        key = ke > key ? ke : key;
+                    }
+                }
+            }
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                key = other > key ? other : key;
+            }
+            if (live && (et & 15) == 0 && key) atomicMax(&s_key[m], key);
+        }
+    } else if constexpr (EPI == EPI_STORE) {
         T *out = reinterpret_cast<T *>(p.out);
         const T *res = reinterpret_cast<const T *>(p.res);
         const bool vec = n0 + nc + 8 <= p.N && (p.ldo & 7) == 0 && ((uintptr_t)out & 15) == 0 &&
@@ -366,6 +399,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __shared__ __align__(8) uint64_t full[kTcMaxStages], empty[kTcMaxStages], acc_full[2], acc_empty[2], done;
     __shared__ uint32_t s_tmem;
     __shared__ int s_bad, s_issued, s_last, s_stop[2], s_counted;
+    __shared__ unsigned long long s_key[EPI == EPI_ARGMAX ? kTcArgmaxRows : 1];  // this CTA's best key per input row
     unsigned char *smem = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int a_bytes = kTileW * kBK * 2, b_bytes = tn * kBK * 2, st_bytes = a_bytes + b_bytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -484,6 +518,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int et = threadIdx.x - 64;  // 0 .. 127 among the epilogue threads
         __nv_bfloat16 *S = reinterpret_cast<__nv_bfloat16 *>(smem + (size_t)nst * st_bytes);
         const bool leader = warp == 2 && lane == 0;
+        if constexpr (EPI == EPI_ARGMAX)
+            for (int m = et; m < kTcArgmaxRows; m += kTcEpiWarps * 32) s_key[m] = 0ull;  // ordered by epi_bar below
         int i = 0;
         for (int u = blockIdx.x; u < sc.nunits; u += gridDim.x, i++) {
             int t, n0, m0, kb, nk;
@@ -534,7 +570,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             v[j] = c0 + j < tn ? ld_f32_early(ws + (size_t)(c0 + j) * 128 + row) : 0.f;
                         tc_epi_stage(S, row, v, brow);
                         epi_bar();
-                        tc_epi_emit<EPI>(p, S, n0, m0 + c0, min(32, tn - c0), et);
+                        tc_epi_emit<EPI>(p, S, n0, m0 + c0, min(32, tn - c0), et, s_key);
 #pragma unroll
                         for (int j = 0; j < 32; j++)
                             if (c0 + j < tn) __stcg(ws + (size_t)(c0 + j) * 128 + row, 0.f);
@@ -557,9 +593,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     tc_epi_stage(S, row, v, brow);
                     epi_bar();
-                    tc_epi_emit<EPI>(p, S, n0, m0 + c0, min(32, tn - c0), et);
+                    tc_epi_emit<EPI>(p, S, n0, m0 + c0, min(32, tn - c0), et, s_key);
                     epi_bar();  // S is rewritten by the next chunk
                 }
+            }
+        }
+        if constexpr (EPI == EPI_ARGMAX) {
+            // every CTA merges its keys (one global atomic per input row) and
+            // arrives, also after a stall; the last to arrive turns the keys
+            // into tokens, advances the lengths (model.cpp:398-407) and
+            // clears the keys and the counter for the next launch
+            epi_bar();
+            for (int m = et; m < p.M; m += kTcEpiWarps * 32)
+                if (s_key[m]) atomicMax(&p.amax_keys[m], s_key[m]);
+            __threadfence();
+            epi_bar();
+            if (leader) s_last = atomicAdd(p.amax_count, 1u) == gridDim.x - 1;
+            epi_bar();
+            if (s_last) {
+                __threadfence();
+                for (int m = et; m < p.M; m += kTcEpiWarps * 32) {
+                    const unsigned long long key = atomicExch(&p.amax_keys[m], 0ull);
+                    const unsigned short u0 = __ldcg(reinterpret_cast<const unsigned short *>(p.out) + (size_t)m * p.ldo);
+                    p.tokens[m] = key_index(key, __uint_as_float((uint32_t)u0 << 16));
+                    if (p.lens && p.lens[m] < p.maxlen) p.lens[m] += 1;
+                }
+                epi_bar();
+                if (leader) atomicExch(p.amax_count, 0u);
             }
         }
     }
@@ -756,6 +816,14 @@ int tc_gemm(const DecodeGemvParams &p0, int epi, cudaStream_t s) {
     if (!p.err) p.err = dev_error_ptr();  // stalls are reported through the device error word
     if (epi == DG_EPI_SWIGLU) return launch_tc<EPI_SWIGLU>(p, s);
     if (epi == DG_EPI_ROPEKV) return launch_tc<EPI_ROPEKV>(p, s);
+    if (epi == DG_EPI_ARGMAX) {
+        WGB_REQUIRE(p.M <= kTcArgmaxRows && !p.bias && !p.res && p.amax_keys && p.amax_count && p.tokens && p.out,
+                    WGB_ERR_INVALID_ARGUMENT, "linear(tc): argmax epilogue needs <= %d rows, its key buffers, no bias",
+                    kTcArgmaxRows);
+        p.tc_ws = nullptr;  // one unit per tile: the keys are merged per CTA
+        p.tc_cnt = nullptr;
+        return launch_tc<EPI_ARGMAX>(p, s);
+    }
     return launch_tc<EPI_STORE>(p, s);
 }
 
@@ -764,6 +832,7 @@ void tc_gemm_prepare() {
     cudaFuncSetAttribute(tc_gemm_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     cudaFuncSetAttribute(tc_gemm_kernel<EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     cudaFuncSetAttribute(tc_gemm_kernel<EPI_ROPEKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(tc_gemm_kernel<EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
 }
 
 bool linear_tc_supported(size_t M, size_t N, size_t K, const void *out, const void *x, const void *w) {

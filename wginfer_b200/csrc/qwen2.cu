@@ -533,8 +533,10 @@ int decode_body(wgbQwen2Model *M, int B, bool ref) {
     }
     for (size_t l = 0; l < m.nlayer; l++)
         if ((rc = run_layer(M, l, B, -1, 0, ref))) return rc;
-    if (!ref && B <= 8) {
-        // final rms_norm + lm_head + greedy argmax + lengths advanced, one launch
+    if (!ref && (B <= 8 || (M->dt == WGINFER_DTYPE_BF16 && B <= 256))) {
+        // final rms_norm + lm_head + greedy argmax + lengths advanced: one
+        // launch up to 8 rows (GEMV), else rms_norm + the tensor-core GEMM
+        // with the argmax epilogue
         DecodeGemvParams p{};
         p.M0 = B;
         p.err = dev_error_ptr();
