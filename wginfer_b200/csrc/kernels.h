@@ -65,14 +65,6 @@ struct DecodeGemvParams {
     // [M0, K] scratch for the normalised rows when more than 8 rows take the
     // tensor-core path with the RMS prologue (may be null: GEMV chunks then)
     void *xn;
-    // split-K scratch of the tensor-core path (may be null: no split): an
-    // f32 accumulator tile per output tile and one arrival counter per
-    // output tile, both zero between launches (the last CTA of a tile
-    // clears them); launches that may overlap need separate scratch
-    float *tc_ws;
-    size_t tc_ws_bytes;
-    unsigned *tc_cnt;
-    int tc_cnt_n;
     // epilogue ARGMAX (the lm_head of a decode step): the logits are stored
     // as with STORE, and each CTA folds its rows' (value, index) keys into
     // amax_keys[m] (zero between launches); the CTA that finishes last writes

@@ -44,6 +44,7 @@ constexpr int kTileW = 128;      // weight rows per CTA (MMA M)
 constexpr int kEpiRows = 32;  // input rows per epilogue chunk
 constexpr size_t kEpiTileBytes = (size_t)kEpiRows * kTileW * 2;  // its bf16 staging tile
 constexpr int kTcArgmaxRows = 256;  // input rows of a fused lm_head + argmax launch
+constexpr int kTcMaxCluster = 16;    // K splits of a tile (a cluster; above 8 where the device allows)
 constexpr long long kTcWaitCycles = 4000000000ll;  // a stage stalled this long (about 2 s) counts as a failure
 
 __device__ __forceinline__ uint32_t s_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -150,11 +151,6 @@ __device__ __forceinline__ uint4 ld_global_v4_early(const void *p) {
     uint4 r;
     asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p) : "memory");
     return r;
-}
-__device__ __forceinline__ float ld_f32_early(const float *p) {
-    float v;
-    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
-    return v;
 }
 __device__ __forceinline__ int64_t ld_s64_early(const int64_t *p) {
     long long v;
@@ -380,6 +376,27 @@ struct TcSched {
     }
 };
 
+// Cluster barrier over every thread of every CTA of the cluster (release /
+// acquire: shared-memory writes before it are visible to the cluster after).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of the same shared-memory location in CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiWarps * 32) : "memory"); }
 __device__ __forceinline__ void mb_arrive(uint64_t *b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s_u32(b)) : "memory");
@@ -398,7 +415,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[kTcMaxStages], empty[kTcMaxStages], acc_full[2], acc_empty[2], done;
     __shared__ uint32_t s_tmem;
-    __shared__ int s_bad, s_issued, s_last, s_stop[2], s_counted;
+    __shared__ int s_bad, s_issued, s_last, s_stop[2];
     __shared__ unsigned long long s_key[EPI == EPI_ARGMAX ? kTcArgmaxRows : 1];  // this CTA's best key per input row
     unsigned char *smem = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int a_bytes = kTileW * kBK * 2, b_bytes = tn * kBK * 2, st_bytes = a_bytes + b_bytes;
@@ -408,7 +425,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (threadIdx.x == 0) {
         s_bad = 0;
         s_issued = 0;
-        s_counted = 0;
         for (int i = 0; i < nst; i++) {
             mb_init(&full[i], 1);
             mb_init(&empty[i], 1);
@@ -539,46 +555,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // this weight row's bias, loaded once per unit
             const float brow = p.bias && n < p.N ? ldf(reinterpret_cast<const T *>(p.bias), n) : 0.f;
             if (sc.ksplit > 1) {
-                // split-K: add this unit's partial tile into the tile's f32
-                // accumulator ([tn][128], lanes contiguous; reductions in L2);
-                // the CTA that arrives last reads the sums, runs the epilogue
-                // and clears the accumulator and the counter for the next launch
-                float *ws = p.tc_ws + (size_t)t * 128 * tn;
+                // split-K: this CTA's partial tile ([tn][128] f32, weight
+                // rows contiguous) goes to its own shared memory, over the
+                // ring (idle: the CTA's only unit has been read by its MMAs);
+                // the cluster reduces the tile after the role branches
+                float *P = reinterpret_cast<float *>(smem);
                 for (int c0 = 0; c0 < tn; c0 += 32) {
                     uint32_t r[32];
                     tmem_ld32(acc + (uint32_t)c0, r);
 #pragma unroll
                     for (int j = 0; j < 32; j++)
-                        if (c0 + j < tn) atomicAdd(ws + (size_t)(c0 + j) * 128 + row, __uint_as_float(r[j]));
+                        if (c0 + j < tn) P[(size_t)(c0 + j) * kTileW + row] = __uint_as_float(r[j]);
                 }
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) mb_arrive(&acc_empty[buf]);
-                __threadfence();
-                epi_bar();
-                if (leader) {
-                    s_last = atomicAdd(&p.tc_cnt[t], 1u) == (unsigned)(sc.ksplit - 1);
-                    s_counted = 1;
-                }
-                epi_bar();
-                if (s_last) {
-                    __threadfence();
-                    for (int c0 = 0; c0 < tn; c0 += 32) {
-                        float v[32];
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            v[j] = c0 + j < tn ? ld_f32_early(ws + (size_t)(c0 + j) * 128 + row) : 0.f;
-                        tc_epi_stage(S, row, v, brow);
-                        epi_bar();
-                        tc_epi_emit<EPI>(p, S, n0, m0 + c0, min(32, tn - c0), et, s_key);
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (c0 + j < tn) __stcg(ws + (size_t)(c0 + j) * 128 + row, 0.f);
-                        epi_bar();  // S is rewritten by the next chunk
-                    }
-                    if (leader) p.tc_cnt[t] = 0;
-                }
-                epi_bar();  // s_last is rewritten by the next unit
             } else {
                 for (int c0 = 0; c0 < tn; c0 += 32) {
                     uint32_t r[32];
@@ -635,20 +626,50 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // the last one issued into each stage before the CTA exits
             for (int it = s_issued - 1; it >= 0 && it >= s_issued - nst; it--)
                 mb_wait(&full[it % nst], (unsigned)((it / nst) & 1));
-            // split-K (one unit per CTA): arrive for the unit if the epilogue
-            // did not, so the tile's counter and accumulator end up cleared
-            if (sc.ksplit > 1 && !s_counted && (int)blockIdx.x < sc.nunits) {
-                int t, n0, m0, kb, nk;
-                sc.unit(blockIdx.x, tn, t, n0, m0, kb, nk);
-                if (atomicAdd(&p.tc_cnt[t], 1u) == (unsigned)(sc.ksplit - 1)) {
-                    float *ws = p.tc_ws + (size_t)t * 128 * tn;
-                    for (int e = 0; e < 128 * tn; e++) __stcg(ws + e, 0.f);
-                    p.tc_cnt[t] = 0;
-                }
-            }
         }
     }
     __syncthreads();
+    if (sc.ksplit > 1) {
+        // split-K over the cluster (the tile's K splits are its consecutive
+        // CTAs, one unit each): every partial tile is in its CTA's shared
+        // memory; CTA z adds the ksplit partials of input rows
+        // [z * per, (z + 1) * per) in split order (a fixed order, so results
+        // do not vary from run to run) through distributed shared memory and
+        // runs the epilogue for them; a second cluster barrier keeps every
+        // CTA's partial tile alive until all have read it
+        cluster_sync_all();
+        if (warp >= 2) {
+            const int row = (warp & 3) * 32 + lane, et = threadIdx.x - 64;
+            const int z = (int)cluster_rank();
+            const int per = (tn + sc.ksplit - 1) / sc.ksplit;
+            const int j0 = min(tn, z * per), j1 = min(tn, j0 + per);
+            int t, n0, m0, kb, nk;
+            sc.unit(blockIdx.x, tn, t, n0, m0, kb, nk);
+            const int n = n0 + row;
+            const float brow = p.bias && n < p.N ? ldf(reinterpret_cast<const T *>(p.bias), n) : 0.f;
+            __nv_bfloat16 *S = reinterpret_cast<__nv_bfloat16 *>(smem + (size_t)nst * st_bytes);
+            uint32_t pq[kTcMaxCluster];  // each split's partial tile, as a cluster shared address
+#pragma unroll
+            for (int q = 0; q < kTcMaxCluster; q++) pq[q] = q < sc.ksplit ? cluster_map(s_u32(smem), q) : 0u;
+            for (int jc = j0; jc < j1; jc += kEpiRows) {
+                const int nr = min(kEpiRows, j1 - jc);
+                for (int j = 0; j < nr; j++) {
+                    const uint32_t off = (uint32_t)(((jc + j) * kTileW + row) * 4);
+                    float x[kTcMaxCluster];
+#pragma unroll
+                    for (int q = 0; q < kTcMaxCluster; q++) x[q] = q < sc.ksplit ? ld_cluster_f32(pq[q] + off) : 0.f;
+                    float acc = 0.f;
+#pragma unroll
+                    for (int q = 0; q < kTcMaxCluster; q++) acc += x[q];
+                    S[j * kTileW + row] = __float2bfloat16_rn(acc + brow);
+                }
+                epi_bar();
+                tc_epi_emit<EPI>(p, S, n0, m0 + jc, nr, et, s_key);
+                epi_bar();  // S is rewritten by the next chunk
+            }
+        }
+        cluster_sync_all();
+    }
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * ncols) : "memory");
@@ -729,25 +750,24 @@ int pick_tn(int M, int N) {
 // Split-K plan: when the weight tiles of the widest input tile (up to 256
 // rows) cannot fill half the SMs (q/k/v, o and down at batch 64 or in a
 // 512-token prefill chunk), keep that tile (the weights are read once, and
-// wide MMAs) and split K across CTAs instead, as many splits as fit in one
-// wave; the
-// partial sums meet in an f32 accumulator in L2 (tc_ws, one [tn][128] tile
-// per output tile, zero between launches). The order in which the splits
-// add up varies from run to run (FAST numerics: f32 sums in any order).
-// Otherwise ksplit = 1 and the input tile comes from pick_tn.
-void plan_split(const DecodeGemvParams &p, int &tn, int &ksplit, int &kper) {
+// wide MMAs) and split K across a cluster of CTAs instead, as many splits as
+// fit in one wave, at most the largest cluster the device schedules for that
+// launch (max_cluster); the partial tiles meet in distributed shared memory.
+// Otherwise ksplit = 1 and the input tile comes from pick_tn. (Splitting
+// gate/up at batch 64 in two, instead of two 32-row input tiles, measured
+// 27.6 against 22.5 us serialised.)
+void plan_split(const DecodeGemvParams &p, bool allow_split, int max_cluster, int &tn, int &ksplit, int &kper) {
     const int ktiles = (p.K + kBK - 1) / kBK;
     ksplit = 1;
     kper = ktiles;
     int wide = 16;
     while (wide < p.M && wide < 256) wide *= 2;
     const long long tiles = (long long)((p.N + kTileW - 1) / kTileW) * ((p.M + wide - 1) / wide);
-    const long long sms = sm_count();
-    if (p.tc_ws && p.tc_cnt && 2 * tiles <= sms && tiles <= p.tc_cnt_n && ktiles >= 2 &&
-        (size_t)tiles * 128 * wide * sizeof(float) <= p.tc_ws_bytes) {
-        int ks = (int)(sms / tiles);
+    const long long sms = sm_count(), slots = sms * tc_ctas_per_sm(wide);  // CTAs of one wave
+    if (allow_split && 2 * tiles <= sms && ktiles >= 2) {
+        int ks = (int)(slots / tiles);
         if (ks > ktiles) ks = ktiles;
-        if (ks > 32) ks = 32;
+        if (ks > max_cluster) ks = max_cluster;
         const int per = (ktiles + ks - 1) / ks;
         ks = (ktiles + per - 1) / per;  // every split gets at least one slice
         if (ks > 1) {
@@ -760,10 +780,46 @@ void plan_split(const DecodeGemvParams &p, int &tn, int &ksplit, int &kper) {
     tn = pick_tn(p.M, p.N);
 }
 
+// Largest cluster of split-K CTAs the device schedules for this kernel at
+// the widest split-K tile (64 input rows, two CTAs per SM), at most
+// kTcMaxCluster; clusters above 8 need the non-portable size attribute. The
+// function attributes are set here (a non-stream call, kept out of graph
+// capture by the first launch).
+template <int EPI> int tc_max_cluster() {
+    static std::atomic<int> cache[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64) {
+        const int c = cache[dev].load(std::memory_order_acquire);
+        if (c) return c;
+    }
+    cudaFuncSetAttribute(tc_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc_smem_max());
+    int best = 8;
+    if (cudaFuncSetAttribute(tc_gemm_kernel<EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(kTcMaxCluster);
+        cfg.blockDim = dim3(kTcThreads);
+        cfg.dynamicSmemBytes = tc_smem_bytes(64);
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = kTcMaxCluster;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxPotentialClusterSize(&n, tc_gemm_kernel<EPI>, &cfg) == cudaSuccess && n > best) best = n;
+    }
+    cudaGetLastError();
+    if (best > kTcMaxCluster) best = kTcMaxCluster;
+    if (dev >= 0 && dev < 64) cache[dev].store(best, std::memory_order_release);
+    return best;
+}
+
 template <int EPI>
 int launch_tc(const DecodeGemvParams &p, cudaStream_t s) {
     int tn, ksplit, kper;
-    plan_split(p, tn, ksplit, kper);
+    plan_split(p, EPI != EPI_ARGMAX, tc_max_cluster<EPI>(), tn, ksplit, kper);
     TcSched sc;
     sc.tiles_m = (p.M + tn - 1) / tn;
     sc.ksplit = ksplit;
@@ -787,17 +843,31 @@ int launch_tc(const DecodeGemvParams &p, cudaStream_t s) {
     }
     cudaLaunchConfig_t cfg = {};
     // persistent: one or two CTAs per SM (the ring takes most of the shared
-    // memory), each taking units blockIdx.x, blockIdx.x + gridDim.x, ...
+    // memory), each taking units blockIdx.x, blockIdx.x + gridDim.x, ...;
+    // split-K: one unit per CTA (the plan keeps them within one wave), the
+    // K splits of a tile as one cluster
     const int cap = sm_count() * tc_ctas_per_sm(tn);
+    if (ksplit > 1 && sc.nunits > cap) return set_error(WGB_ERR_UNSUPPORTED, "linear(tc): split-K plan exceeds one wave");
     cfg.gridDim = dim3((unsigned)(sc.nunits < cap ? sc.nunits : cap));
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = tc_smem_bytes(tn);
     cfg.stream = s;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (pdl_enabled()) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (ksplit > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = (unsigned)ksplit;
+        at[na].val.clusterDim.y = 1;
+        at[na].val.clusterDim.z = 1;
+        na++;
+    }
     cfg.attrs = at;
-    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cfg.numAttrs = na;
     cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI>, tmW, tmX, p, tn, tc_stages(tn), sc);
     if (e != cudaSuccess) return set_error(WGB_ERR_CUDA, "linear(tc): %s", cudaGetErrorString(e));
     return WGB_OK;
@@ -820,8 +890,6 @@ int tc_gemm(const DecodeGemvParams &p0, int epi, cudaStream_t s) {
         WGB_REQUIRE(p.M <= kTcArgmaxRows && !p.bias && !p.res && p.amax_keys && p.amax_count && p.tokens && p.out,
                     WGB_ERR_INVALID_ARGUMENT, "linear(tc): argmax epilogue needs <= %d rows, its key buffers, no bias",
                     kTcArgmaxRows);
-        p.tc_ws = nullptr;  // one unit per tile: the keys are merged per CTA
-        p.tc_cnt = nullptr;
         return launch_tc<EPI_ARGMAX>(p, s);
     }
     return launch_tc<EPI_STORE>(p, s);
@@ -833,6 +901,10 @@ void tc_gemm_prepare() {
     cudaFuncSetAttribute(tc_gemm_kernel<EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     cudaFuncSetAttribute(tc_gemm_kernel<EPI_ROPEKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     cudaFuncSetAttribute(tc_gemm_kernel<EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    tc_max_cluster<EPI_STORE>();  // the cluster limits are settled outside any graph capture
+    tc_max_cluster<EPI_SWIGLU>();
+    tc_max_cluster<EPI_ROPEKV>();
+    tc_max_cluster<EPI_ARGMAX>();
 }
 
 bool linear_tc_supported(size_t M, size_t N, size_t K, const void *out, const void *x, const void *w) {

@@ -122,9 +122,6 @@ struct LayerW {
 // Split-K scratch of the tensor-core projections (up to 64 rows): one region
 // per call site of a layer (q/k/v, o, gate/up, down, lm_head), so launches
 // that the dependent-launch chain lets start early never share one.
-constexpr int kTcSites = 5;
-constexpr size_t kTcWsBytes = 4u << 20;  // f32 accumulator tiles per site
-constexpr int kTcCounters = 256;         // arrival counters per site
 
 struct wgbQwen2Model {
     wgbQwen2Meta m;
@@ -145,8 +142,6 @@ struct wgbQwen2Model {
     // activations (rows = max(max_batch, chunk))
     void *x, *xn, *qkv, *qr, *att, *gu, *act, *logits;
     void *attn_ws;
-    float *tc_ws;      // [kTcSites] split-K accumulators (zero between launches)
-    unsigned *tc_cnt;  // [kTcSites][kTcCounters] arrival counters (zero between launches)
     unsigned long long *amax_keys;  // [max_batch] fused lm_head + argmax keys (zero between launches)
     unsigned *amax_count;           // its CTA arrival counter (zero between launches)
     size_t attn_ws_bytes;
@@ -255,13 +250,6 @@ int run_layer_ref(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t tot
     return linear_forward(M->dt, M->x, M->act, w.down_w, nullptr, M->x, T, hs, di, ref, s);
 }
 
-// Split-K scratch of call site `site` for the tensor-core path.
-void set_tc_scratch(const wgbQwen2Model *M, DecodeGemvParams &p, int site) {
-    p.tc_ws = M->tc_ws + (size_t)site * (kTcWsBytes / sizeof(float));
-    p.tc_ws_bytes = kTcWsBytes;
-    p.tc_cnt = M->tc_cnt + (size_t)site * kTcCounters;
-    p.tc_cnt_n = kTcCounters;
-}
 
 // The same layer in FAST numerics: five launches, each chained to the
 // previous one by programmatic dependent launch (decode_gemv.cu).
@@ -305,7 +293,6 @@ int run_layer_fast(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t to
     p.maxseq = (int)m.maxseq;
     p.prefill_seq = prefill_seq;
     p.xn = M->xn;
-    set_tc_scratch(M, p, 0);
     if ((rc = decode_gemv(M->dt, p, DG_PRO_RMS, DG_EPI_ROPEKV, s))) return rc;
     WGB_TRACE("qkv_gemv+rms+rope+kv");
     // no L2 prefetch from attention: its own K/V reads are latency-critical
@@ -324,7 +311,6 @@ int run_layer_fast(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t to
     o.res = M->x;
     o.pf_ptr[0] = w.down_w;
     o.pf_bytes[0] = down_b;
-    set_tc_scratch(M, o, 1);
     if ((rc = decode_gemv(M->dt, o, DG_PRO_PLAIN, DG_EPI_STORE, s))) return rc;
     WGB_TRACE("o_gemv+residual");
     // rms_norm + gate/up projection + SwiGLU
@@ -343,7 +329,6 @@ int run_layer_fast(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t to
     g.pf_ptr[0] = next_qkv;
     g.pf_bytes[0] = next_qkv_b;
     g.xn = M->xn;
-    set_tc_scratch(M, g, 2);
     if ((rc = decode_gemv(M->dt, g, DG_PRO_RMS, DG_EPI_SWIGLU, s))) return rc;
     WGB_TRACE("gate_up_gemv+rms+swiglu");
     // down_proj + residual
@@ -366,7 +351,6 @@ int run_layer_fast(wgbQwen2Model *M, size_t l, int T, int prefill_seq, size_t to
         d.pf_ptr[0] = (const char *)M->out_embed + next_qkv_b;
         d.pf_bytes[0] = std::min<size_t>(m.voc * m.hs * es - next_qkv_b, 32u << 20);
     }
-    set_tc_scratch(M, d, 3);
     rc = decode_gemv(M->dt, d, DG_PRO_PLAIN, DG_EPI_STORE, s);
     WGB_TRACE("down_gemv+residual");
     return rc;
@@ -495,7 +479,6 @@ int lm_head(wgbQwen2Model *M, const void *x_row, int rows, void *logits, bool re
     p.out = logits;
     p.ldo = (int)m.voc;
     p.xn = M->xn;
-    set_tc_scratch(M, p, 4);
     return decode_gemv(M->dt, p, DG_PRO_RMS, DG_EPI_STORE, s);
 }
 
@@ -712,8 +695,6 @@ int wgb_qwen2_create(const wgbQwen2Meta *meta, int device, int max_batch, wgbQwe
     items.push_back({&M->act, rows * m.di * es});
     items.push_back({&M->logits, (size_t)max_batch * m.voc * es});
     items.push_back({&M->attn_ws, M->attn_ws_bytes});
-    items.push_back({(void **)&M->tc_ws, kTcSites * kTcWsBytes});
-    items.push_back({(void **)&M->tc_cnt, (size_t)kTcSites * kTcCounters * sizeof(unsigned)});
     items.push_back({(void **)&M->amax_keys, (size_t)max_batch * sizeof(unsigned long long)});
     items.push_back({(void **)&M->amax_count, sizeof(unsigned)});
 
