@@ -81,6 +81,81 @@ def test_stream_fast_numerics_teacher_forced(cuda, name):
     print(f"{name}: FAST teacher-forced agreement {agree:.3f}")
 
 
+def _bf16_ulp(x):
+    """Spacing of bf16 values at magnitude x (8 significant bits)."""
+    return np.exp2(np.floor(np.log2(np.maximum(np.abs(x), 2.0 ** -126))) - 7)
+
+
+def _fast_against_reference(F, R, what):
+    """FAST and REFERENCE compute the same bf16 ops and differ only in the
+    order of their f32 sums, which moves a rounded result by at most an ulp
+    here and there. Bound: each FAST logit row stays within 2 bf16 ulps of the
+    row's largest |logit| of the REFERENCE row (REFERENCE is bit-identical to
+    the reference's CPU backend); measured 1 ulp on the tiny model, config 2
+    and config 4. Where the REFERENCE top-2 margin is above twice that bound,
+    the greedy tokens must agree."""
+    bound = 2 * _bf16_ulp(np.abs(R).max(axis=1))
+    err = np.abs(F - R).max(axis=1)
+    worst = int(np.argmax(err / bound))
+    assert np.all(err <= bound), f"{what}: row {worst} FAST error {err[worst]} > bound {bound[worst]}"
+    srt = np.sort(R, axis=1)
+    margin = srt[:, -1] - srt[:, -2]
+    sure = margin > 2 * bound
+    assert np.array_equal(F.argmax(1)[sure], R.argmax(1)[sure]), f"{what}: greedy token differs at a clear margin"
+
+
+@pytest.mark.parametrize("name", ["tiny_p100_g32", "one_layer_p512_g128"])
+def test_fast_logits_within_two_bf16_ulps_teacher_forced(cuda, name):
+    """Config 2 (one layer, 512-token prompt, 128 decode steps) and the tiny
+    model, teacher-forced on the golden stream in both numerics: every step's
+    FAST logits against REFERENCE logits (see _fast_against_reference)."""
+    cfg, plen, steps = CS.SMALL_MODELS[name]
+    gold = STREAMS[name]["tokens"]
+    m = model(cfg)
+
+    def run():
+        m.reset_cache()
+        m.infer(CS.prompt(plen, cfg.voc))
+        rows = [m.logits(0).copy()]
+        for t in gold[:steps - 1]:
+            m.infer([t])
+            rows.append(m.logits(0).copy())
+        return np.stack(rows)
+
+    with numerics("reference"):
+        R = run()
+    with numerics("fast"):
+        F = run()
+    _fast_against_reference(F, R, name)
+
+
+def test_fast_logits_within_two_bf16_ulps_batched_64(cuda):
+    """Config 4 (64 sequences x 2048-token prompts, one layer): the logits of
+    every sequence after its prefill (tensor-core GEMMs with 256-row input
+    tiles, tensor-core prefill attention) and after the first batch-64 decode
+    step (split-K cluster GEMMs, TMA-ring decode attention, the lm_head GEMM
+    with the argmax epilogue), FAST against REFERENCE."""
+    spec = CS.BATCHED["one_layer_bs64_p2048"]
+    B = spec["sequences"]
+    ids = CS.batched_prompts(spec)
+    m = model(spec["cfg"], max_batch=B)
+    out = {}
+    for mode in ("reference", "fast"):
+        with numerics(mode):
+            m.reset_cache()
+            for b in range(B):
+                m.prefill(b, ids[b])
+            after_prefill = np.stack([m.logits(b) for b in range(B)])
+            first = m.tokens(B)
+            m.decode_step(B)
+            out[mode] = (after_prefill, np.stack([m.logits(b) for b in range(B)]), first)
+    (R0, R1, rt), (F0, F1, ft) = out["reference"], out["fast"]
+    _fast_against_reference(F0, R0, "after prefill")
+    same = np.array(rt) == np.array(ft)  # the step's input is the sequence's first token
+    assert same.sum() >= B // 2
+    _fast_against_reference(F1[same], R1[same], "first decode step")
+
+
 def test_batched_64_sequences_2048_prompts_reference_numerics(cuda):
     """64 sequences with 2048-token prompts decoded together on the one-layer
     model, in REFERENCE numerics, through the batch-64 decode graph: the
