@@ -19,6 +19,7 @@
 
 #include <atomic>
 
+#include "argmax_key.cuh"
 #include "common.cuh"
 
 namespace cg = cooperative_groups;
@@ -34,13 +35,6 @@ constexpr int kThreadsWide = 512, kThreadsFew = 256;
 // a few rows, where a 151936-wide bf16 row on 8 CTAs is then one round trip
 // (latency, not bandwidth, is what a few rows pay for)
 constexpr int kBWide = 8, kBFew = 10;
-
-__device__ __forceinline__ unsigned long long make_key(float v, uint32_t idx) {
-    if (v == 0.f) v = 0.f;  // -0 -> +0
-    uint32_t u = __float_as_uint(v);
-    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
-}
 
 // Per-thread running best over the thread's elements, which it visits in
 // increasing index order: strict '>' keeps the first index of a tie, and NaN
