@@ -498,6 +498,35 @@ def bs64(args, world, rank, local):
             "workload": "one-layer Qwen2 (the config-2 layer + embeddings + lm_head), bf16, greedy"}
 
 
+def prefill_only(plen: int, reps: int) -> dict:
+    """One sequence's prefill of `plen` tokens on the 28-layer model (FAST
+    numerics, one GPU): CUDA events on the model's stream around
+    wgb_qwen2_prefill, the best of `reps` after one warm-up."""
+    import torch
+    from wginfer_b200 import numerics
+    from wginfer_b200.synthetic import Qwen2Config, prompt_ids
+    cfg = Qwen2Config(nlayer=28, maxseq=plen + 64)
+    with numerics("fast"):
+        m, _ = build_model(cfg, 1, 0)
+        ids = prompt_ids(plen, cfg.voc, seed=0).numpy()
+        st = m.torch_stream()
+        times = []
+        for r in range(reps + 1):
+            m.reset_cache()
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(st)
+            m.prefill(0, ids)
+            e.record(st)
+            torch.cuda.synchronize()
+            if r:
+                times.append(s.elapsed_time(e) / 1e3)
+        m.close()
+    best = min(times)
+    return {"prompt": plen, "value": round(plen / best, 1), "unit": "tok/s", "ms": round(best * 1e3, 3),
+            "reps": reps, "workload": "28-layer Qwen2-1.5B architecture, bf16, FAST, one sequence"}
+
+
 # ---------------------------------------------------------------- reference CPU arm
 def reference_model():
     """The reference's own Model (oracle/_ref, its CPU device) with the
@@ -591,6 +620,8 @@ def main():
     ap.add_argument("--no-bs64", action="store_true")
     ap.add_argument("--only-bs64", action="store_true",
                     help="print only the batched-decode result (64 sequences x 2048-token prompts)")
+    ap.add_argument("--only-prefill", type=int, default=0, metavar="TOKENS",
+                    help="print only the time of one prefill of this many tokens (28-layer model, one GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op-probe", choices=["add", "swiglu", "rms_norm", "argmax"], default=None,
                     help="only launch one swept op a few times at >= 64 MB (for an ncu capture)")
@@ -604,6 +635,9 @@ def main():
         args.warmup = 3
     if args.op_probe:
         op_probe(args.op_probe)
+    elif args.only_prefill:
+        print(json.dumps({"metric": "prefill tok/s", "prefill": prefill_only(args.only_prefill, max(1, args.steps))}),
+              flush=True)
     elif args.impl == "reference":
         run_reference(args)
     elif args.only_bs64:
