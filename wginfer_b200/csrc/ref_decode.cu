@@ -41,11 +41,12 @@
 //
 // ref_attn_decode_kernel — one query row (the newest token of a sequence)
 //   against its cached keys, per (sequence, head), on a cluster of 8 CTAs:
-//   scores (a d-long chain per key) split over the cluster and gathered in
-//   CTA 0 through distributed shared memory; CTA 0 takes the max, exp, the
-//   L-long sequential sum and the division; every CTA then runs 16 of the
-//   128 output columns' L-long chains of round(p * v) over its V column
-//   slice, copied into shared memory while the scores were computed.
+//   scores (a d-long chain per key) split over the cluster and written to
+//   every CTA through distributed shared memory (one cluster barrier); every
+//   CTA takes the max, exp, the L-long sequential sum and the division
+//   itself (the same operations in the same order as its peers), then runs
+//   16 of the 128 output columns' L-long chains of round(p * v) over its V
+//   column slice, copied into shared memory while the scores were computed.
 #include <cooperative_groups.h>
 #include <cuda_pipeline.h>
 
@@ -572,7 +573,13 @@ __global__ void __launch_bounds__(kRaThreads) ref_attn_decode_kernel(const T *__
     // loaded together (one round trip; plain coherent loads, both were
     // written by the previous kernel), the query kept as 16-byte vectors of
     // T for the chain steps.
-    float *sc0 = cluster.map_shared_rank(sc, 0);
+    // every score goes to every CTA of the cluster, which then runs the
+    // softmax itself (the same operations in the same order, so the same
+    // bits in every CTA): one cluster barrier instead of three and no copy
+    // of the probabilities out of CTA 0
+    float *scr[kRaCluster];
+#pragma unroll
+    for (int c = 0; c < kRaCluster; c++) scr[c] = cluster.map_shared_rank(sc, c);
     const int per = (L + kRaCluster - 1) / kRaCluster;
     const int j0 = r * per, j1 = min(L, j0 + per);
     const uint4 *qrow = reinterpret_cast<const uint4 *>(q + ((size_t)b * nh + h) * DH);
@@ -593,12 +600,16 @@ __global__ void __launch_bounds__(kRaThreads) ref_attn_decode_kernel(const T *__
             chain_vec<T>(aa, qv[u], ka[u]);
             chain_vec<T>(ab, qv[u], kbv[u]);
         }
-        sc0[ja] = __fmul_rn(scale, aa);
-        if (hb) sc0[jb] = __fmul_rn(scale, ab);
+        const float sa = __fmul_rn(scale, aa), sb = __fmul_rn(scale, ab);
+#pragma unroll
+        for (int c = 0; c < kRaCluster; c++) {
+            scr[c][ja] = sa;
+            if (hb) scr[c][jb] = sb;
+        }
     }
-    cluster.sync();  // every score is in CTA 0
+    cluster.sync();  // every score is in every CTA; no CTA reads another's shared memory after this
 
-    if (r == 0) {
+    {
         // softmax (self_attention_cpu.cpp:63-77): max, exp(s - max), a
         // sequential sum over every key, then one division per key
         float mx = -FLT_MAX;
@@ -632,12 +643,6 @@ __global__ void __launch_bounds__(kRaThreads) ref_attn_decode_kernel(const T *__
         const float sum = s_sum;
         for (int j = tid; j < L; j += kRaThreads) sc[j] = __fdiv_rn(sc[j], sum);
     }
-    cluster.sync();  // the probabilities are final in CTA 0
-    if (r != 0) {
-        for (int i = tid; i < L / 4; i += kRaThreads)
-            reinterpret_cast<float4 *>(sc)[i] = reinterpret_cast<const float4 *>(sc0)[i];
-        for (int j = (L / 4) * 4 + tid; j < L; j += kRaThreads) sc[j] = sc0[j];
-    }
     __pipeline_wait_prior(0);
     __syncthreads();
     // output (self_attention_cpu.cpp:81-89): per column a sequential sum over
@@ -668,7 +673,6 @@ __global__ void __launch_bounds__(kRaThreads) ref_attn_decode_kernel(const T *__
         for (; j < L; j++) acc = __fadd_rn(acc, __fmul_rn(sc[j], Elem<T>::load(vs[(size_t)j * COLS + tid])));
         stf(out, ((size_t)b * nh + h) * DH + r * COLS + tid, acc);
     }
-    cluster.sync();  // CTA 0's shared memory stays until every CTA has read it
 }
 
 template <typename T, int DH> void ra_set_attr() {
