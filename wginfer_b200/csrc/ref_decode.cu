@@ -552,48 +552,65 @@ __global__ void __launch_bounds__(kRaThreads) ref_attn_decode_kernel(const T *__
     T *vs = reinterpret_cast<T *>(sc + ra_scores_len(maxlen));         // [maxlen][COLS]
 
     pdl_trigger();
-    pdl_wait();  // q and the newest K/V row come from the previous kernel
+    // the lengths were set by an earlier step; the cached rows other than
+    // the newest were written by earlier steps too, so they are requested
+    // before the wait for the previous kernel (which writes q and the newest
+    // K/V row)
     long Ll = lens[b] + 1;
     if (Ll > maxlen) Ll = maxlen;
     if (Ll < 1) Ll = 1;
-    const int L = (int)Ll;
+    const int L = (int)Ll, newest = L - 1;
     const size_t rstride = (size_t)nkvh * DH;  // elements between cached positions
     const T *kb = kcache + (size_t)b * seq_stride + (size_t)kvh * DH;
     const T *vb = vcache + (size_t)b * seq_stride + (size_t)kvh * DH + r * COLS;
     // this CTA's V columns, all positions, into shared memory (needed last)
     for (int i = tid; i < L * (COLS / V); i += kRaThreads) {
         const int j = i / (COLS / V), c = i - j * (COLS / V);
-        __pipeline_memcpy_async(vs + (size_t)j * COLS + c * V, vb + (size_t)j * rstride + c * V, 16);
+        if (j != newest) __pipeline_memcpy_async(vs + (size_t)j * COLS + c * V, vb + (size_t)j * rstride + c * V, 16);
     }
-    __pipeline_commit();
-
     // scores (self_attention_cpu.cpp:37-45): scale * (sequential dot over d);
     // this CTA's keys are [j0, j1), one key per thread per pass, two passes
-    // interleaved; each score goes to CTA 0. The key rows and the query are
-    // loaded together (one round trip; plain coherent loads, both were
-    // written by the previous kernel), the query kept as 16-byte vectors of
-    // T for the chain steps.
-    // every score goes to every CTA of the cluster, which then runs the
-    // softmax itself (the same operations in the same order, so the same
-    // bits in every CTA): one cluster barrier instead of three and no copy
-    // of the probabilities out of CTA 0
+    // interleaved, the first pass's key rows loaded before the wait. Every
+    // score goes to every CTA of the cluster, which then runs the softmax
+    // itself (the same operations in the same order, so the same bits in
+    // every CTA): one cluster barrier and no copy of the probabilities.
     float *scr[kRaCluster];
 #pragma unroll
     for (int c = 0; c < kRaCluster; c++) scr[c] = cluster.map_shared_rank(sc, c);
     const int per = (L + kRaCluster - 1) / kRaCluster;
     const int j0 = r * per, j1 = min(L, j0 + per);
+    uint4 ka[VPR], kbv[VPR];
+    auto load_rows = [&](int ja, int jb, bool early) {
+#pragma unroll
+        for (int u = 0; u < VPR; u++) {
+            if (ja < j1 && (ja != newest) == early) ka[u] = *reinterpret_cast<const uint4 *>(kb + (size_t)ja * rstride + u * V);
+            if (jb < j1 && (jb != newest) == early) kbv[u] = *reinterpret_cast<const uint4 *>(kb + (size_t)jb * rstride + u * V);
+        }
+    };
+#pragma unroll
+    for (int u = 0; u < VPR; u++) ka[u] = kbv[u] = make_uint4(0u, 0u, 0u, 0u);
+    load_rows(j0 + tid, j0 + tid + kRaThreads, true);
+    pdl_wait();
+    for (int i = tid; i < COLS / V; i += kRaThreads)
+        if (newest < L) __pipeline_memcpy_async(vs + (size_t)newest * COLS + i * V, vb + (size_t)newest * rstride + i * V, 16);
+    __pipeline_commit();
     const uint4 *qrow = reinterpret_cast<const uint4 *>(q + ((size_t)b * nh + h) * DH);
     for (int ja = j0 + tid; ja < j1; ja += 2 * kRaThreads) {
         const int jb = ja + kRaThreads;
         const bool hb = jb < j1;
-        uint4 ka[VPR], kbv[VPR], qv[VPR];
+        if (ja == j0 + tid) {
+            load_rows(ja, jb, false);  // the newest row, if it is one of these
+        } else {
 #pragma unroll
-        for (int u = 0; u < VPR; u++) {
-            ka[u] = *reinterpret_cast<const uint4 *>(kb + (size_t)ja * rstride + u * V);
-            kbv[u] = hb ? *reinterpret_cast<const uint4 *>(kb + (size_t)jb * rstride + u * V)
-                        : make_uint4(0u, 0u, 0u, 0u);
-            qv[u] = qrow[u];
+            for (int u = 0; u < VPR; u++) {
+                ka[u] = *reinterpret_cast<const uint4 *>(kb + (size_t)ja * rstride + u * V);
+                kbv[u] = hb ? *reinterpret_cast<const uint4 *>(kb + (size_t)jb * rstride + u * V)
+                            : make_uint4(0u, 0u, 0u, 0u);
+            }
         }
+        uint4 qv[VPR];
+#pragma unroll
+        for (int u = 0; u < VPR; u++) qv[u] = qrow[u];
         float aa = 0.f, ab = 0.f;
 #pragma unroll
         for (int u = 0; u < VPR; u++) {
