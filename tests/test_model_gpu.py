@@ -73,7 +73,7 @@ def test_stream_fast_numerics_teacher_forced(cuda, name):
     got = [m.infer(CS.prompt(plen, cfg.voc))]
     for t in gold[:-1]:
         got.append(m.infer([t]))  # teacher forcing on the golden stream
-    bound = 0.125  # FAST logit error stays below this on these models (measured: <= 0.11)
+    bound = 0.125  # token agreement asserted only above this golden margin (FAST logit error: see the ulp tests)
     for i, (a, b, mg) in enumerate(zip(got, gold, margins)):
         if mg > bound:
             assert a == b, f"step {i}: margin {mg} but tokens differ"
@@ -86,15 +86,16 @@ def _bf16_ulp(x):
     return np.exp2(np.floor(np.log2(np.maximum(np.abs(x), 2.0 ** -126))) - 7)
 
 
-def _fast_against_reference(F, R, what):
+def _fast_against_reference(F, R, what, ulps=2):
     """FAST and REFERENCE compute the same bf16 ops and differ only in the
     order of their f32 sums, which moves a rounded result by at most an ulp
-    here and there. Bound: each FAST logit row stays within 2 bf16 ulps of the
-    row's largest |logit| of the REFERENCE row (REFERENCE is bit-identical to
-    the reference's CPU backend); measured 1 ulp on the tiny model, config 2
-    and config 4. Where the REFERENCE top-2 margin is above twice that bound,
-    the greedy tokens must agree."""
-    bound = 2 * _bf16_ulp(np.abs(R).max(axis=1))
+    here and there per op. Bound: each FAST logit row stays within `ulps` bf16
+    ulps of the row's largest |logit| of the REFERENCE row (REFERENCE is
+    bit-identical to the reference's CPU backend): 2 for one layer (measured
+    1 on the tiny model, config 2 and config 4), 12 for 28 layers (measured
+    up to 9.4, the differences of 28 layers adding up). Where the REFERENCE
+    top-2 margin is above twice the bound, the greedy tokens must agree."""
+    bound = ulps * _bf16_ulp(np.abs(R).max(axis=1))
     err = np.abs(F - R).max(axis=1)
     worst = int(np.argmax(err / bound))
     assert np.all(err <= bound), f"{what}: row {worst} FAST error {err[worst]} > bound {bound[worst]}"
@@ -104,12 +105,13 @@ def _fast_against_reference(F, R, what):
     assert np.array_equal(F.argmax(1)[sure], R.argmax(1)[sure]), f"{what}: greedy token differs at a clear margin"
 
 
-@pytest.mark.parametrize("name", ["tiny_p100_g32", "one_layer_p512_g128"])
-def test_fast_logits_within_two_bf16_ulps_teacher_forced(cuda, name):
-    """Config 2 (one layer, 512-token prompt, 128 decode steps) and the tiny
-    model, teacher-forced on the golden stream in both numerics: every step's
-    FAST logits against REFERENCE logits (see _fast_against_reference)."""
-    cfg, plen, steps = CS.SMALL_MODELS[name]
+@pytest.mark.parametrize("name,ulps", [("tiny_p100_g32", 2), ("one_layer_p512_g128", 2), ("qwen2_1p5b_p512_g128", 12)])
+def test_fast_logits_within_bf16_ulps_teacher_forced(cuda, name, ulps):
+    """Config 2 (one layer, 512-token prompt, 128 decode steps), config 3 (28
+    layers, same prompt and steps) and the tiny model, teacher-forced on the
+    golden stream in both numerics: every step's FAST logits against
+    REFERENCE logits (see _fast_against_reference)."""
+    cfg, plen, steps = (CS.SMALL_MODELS.get(name) or CS.FULL_MODELS[name])[:3]
     gold = STREAMS[name]["tokens"]
     m = model(cfg)
 
@@ -126,7 +128,7 @@ def test_fast_logits_within_two_bf16_ulps_teacher_forced(cuda, name):
         R = run()
     with numerics("fast"):
         F = run()
-    _fast_against_reference(F, R, name)
+    _fast_against_reference(F, R, name, ulps)
 
 
 def test_fast_logits_within_two_bf16_ulps_batched_64(cuda):
