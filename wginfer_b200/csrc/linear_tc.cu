@@ -17,8 +17,12 @@
 // from the neighbouring lane by shuffle), while the next unit's MMAs fill
 // the other accumulator. The epilogue stages each 32-input-row chunk as
 // bf16 in shared memory and then writes it (and reads residuals) in 16-byte
-// pieces of 8 adjacent outputs. Roofline: tensor, 2*M*N*K
-// flops (HBM for a few input rows: the weights, N*K*2 bytes).
+// pieces of 8 adjacent outputs. When a tile's weight rows cannot fill the
+// GPU (narrow projections), its K range is split over a cluster of CTAs
+// whose partial tiles meet in distributed shared memory (plan_split); the
+// lm_head of a decode step can fold the greedy argmax into its epilogue
+// (EPI_ARGMAX). Roofline: tensor, 2*M*N*K flops (HBM for a few input rows:
+// the weights, N*K*2 bytes).
 //
 // Every mbarrier wait is bounded; on a stall the kernel records an error in
 // the device error word, skips the rest, waits (bounded) for copies in

@@ -119,10 +119,6 @@ struct LayerW {
     void *attn_norm, *qkv_w, *qkv_b, *o_w, *mlp_norm, *gu_w, *down_w;
 };
 
-// Split-K scratch of the tensor-core projections (up to 64 rows): one region
-// per call site of a layer (q/k/v, o, gate/up, down, lm_head), so launches
-// that the dependent-launch chain lets start early never share one.
-
 struct wgbQwen2Model {
     wgbQwen2Meta m;
     int device = 0, max_batch = 1, chunk = 1;
