@@ -752,6 +752,10 @@ namespace {
 // only while the grid would leave more than half the CTA slots idle (two per
 // SM for tiles up to 64 rows): each halving
 // re-reads the weights once more (from L2) and makes every MMA narrower.
+// (Choosing instead, above 128 rows, the tile with the fewest operand bytes
+// per SM, 64-row tiles for q/k/v, o and down at 512 rows, measured slower:
+// 4.74 against 4.63 ms for the 512-token prefill; a unit with a long K range
+// is bound by the bytes its ring keeps in flight, not by L2.)
 int pick_tn(int M, int N) {
     int tn = 16;
     while (tn < M && tn < 256) tn *= 2;
@@ -760,15 +764,22 @@ int pick_tn(int M, int N) {
     return tn;
 }
 
-// Split-K plan: when the weight tiles of the widest input tile (up to 256
-// rows) cannot fill half the SMs (q/k/v, o and down at batch 64 or in a
-// 512-token prefill chunk), keep that tile (the weights are read once, and
-// wide MMAs) and split K across a cluster of CTAs instead, as many splits as
-// fit in one wave, at most the largest cluster the device schedules for that
-// launch (max_cluster); the partial tiles meet in distributed shared memory.
-// Otherwise ksplit = 1 and the input tile comes from pick_tn. (Splitting
-// gate/up at batch 64 in two, instead of two 32-row input tiles, measured
-// 27.6 against 22.5 us serialised.)
+// Split-K plan: when the weight tiles of the widest input tile (up to 128
+// rows) cannot fill half the SMs (q/k/v, o and down at batch 64, or in a
+// prefill chunk of up to 128 tokens), keep that tile (the weights are read
+// once, and wide MMAs) and split K across a cluster of CTAs instead, as many
+// splits as fit in one wave, at most the largest cluster the device
+// schedules for that launch (max_cluster); the partial tiles meet in
+// distributed shared memory. Otherwise ksplit = 1 and the input tile comes
+// from pick_tn. Above 128 input rows the partial tile of a 256-row input
+// tile (128 KB of f32 per CTA) makes the cluster reduction cost more than
+// the narrower input tiles of the unsplit plan: a 512-token prefill of the
+// 28-layer Qwen2-1.5B shapes took 5.39-5.41 ms split and 4.63-4.66 ms
+// unsplit (a 256-token one 4.08 against 3.93 ms), while a 128-token one took
+// 3.09-3.15 ms split and 3.53 ms unsplit. The down projection alone (K =
+// 8960) is the exception at 512 rows: 55.8 us split, 63.7 us unsplit.
+// (Splitting gate/up at batch 64 in two, instead of two 32-row input tiles,
+// measured 27.6 against 22.5 us serialised.)
 void plan_split(const DecodeGemvParams &p, bool allow_split, int max_cluster, int &tn, int &ksplit, int &kper) {
     const int ktiles = (p.K + kBK - 1) / kBK;
     ksplit = 1;
@@ -777,7 +788,7 @@ void plan_split(const DecodeGemvParams &p, bool allow_split, int max_cluster, in
     while (wide < p.M && wide < 256) wide *= 2;
     const long long tiles = (long long)((p.N + kTileW - 1) / kTileW) * ((p.M + wide - 1) / wide);
     const long long sms = sm_count(), slots = sms * tc_ctas_per_sm(wide);  // CTAs of one wave
-    if (allow_split && 2 * tiles <= sms && ktiles >= 2) {
+    if (allow_split && wide <= 128 && 2 * tiles <= sms && ktiles >= 2) {
         int ks = (int)(slots / tiles);
         if (ks > ktiles) ks = ktiles;
         if (ks > max_cluster) ks = max_cluster;
