@@ -764,20 +764,21 @@ int pick_tn(int M, int N) {
     return tn;
 }
 
-// Split-K plan: when the weight tiles of the widest input tile (up to 128
-// rows) cannot fill half the SMs (q/k/v, o and down at batch 64, or in a
-// prefill chunk of up to 128 tokens), keep that tile (the weights are read
-// once, and wide MMAs) and split K across a cluster of CTAs instead, as many
-// splits as fit in one wave, at most the largest cluster the device
-// schedules for that launch (max_cluster); the partial tiles meet in
-// distributed shared memory. Otherwise ksplit = 1 and the input tile comes
-// from pick_tn. Above 128 input rows the partial tile of a 256-row input
-// tile (128 KB of f32 per CTA) makes the cluster reduction cost more than
-// the narrower input tiles of the unsplit plan: a 512-token prefill of the
-// 28-layer Qwen2-1.5B shapes took 5.39-5.41 ms split and 4.63-4.66 ms
-// unsplit (a 256-token one 4.08 against 3.93 ms), while a 128-token one took
-// 3.09-3.15 ms split and 3.53 ms unsplit. The down projection alone (K =
-// 8960) is the exception at 512 rows: 55.8 us split, 63.7 us unsplit.
+// Split-K plan: when the weight tiles of the widest input tile cannot fill
+// half the SMs, keep that tile (the weights are read once, and wide MMAs)
+// and split K across a cluster of CTAs instead, as many splits as fit in one
+// wave, at most the largest cluster the device schedules for that launch
+// (max_cluster); the partial tiles meet in distributed shared memory.
+// Otherwise ksplit = 1 and the input tile comes from pick_tn.
+// Up to 128 input rows (q/k/v, o and down at batch 64, prefill chunks of up
+// to 128 tokens) every such projection splits. Above, a 256-row input tile's
+// partial (128 KB of f32 per CTA) makes the cluster reduction cost more than
+// the unsplit plan's narrower input tiles unless K is long and the split is
+// at least 4 ways; of the Qwen2-1.5B shapes that keeps only down (K = 8960)
+// split, at 256 and 512 rows. Measured on the 28-layer prefill (ms; every
+// projection split / none split / down split only): 128 tokens 3.09-3.15 /
+// 3.53 / -, 256 tokens 4.08 / 3.93 / 3.24, 512 tokens 5.39-5.41 / 4.63-4.66 /
+// 4.43; at 1024 tokens down splits 3 ways: 7.06 split against 6.33 unsplit.
 // (Splitting gate/up at batch 64 in two, instead of two 32-row input tiles,
 // measured 27.6 against 22.5 us serialised.)
 void plan_split(const DecodeGemvParams &p, bool allow_split, int max_cluster, int &tn, int &ksplit, int &kper) {
@@ -788,7 +789,8 @@ void plan_split(const DecodeGemvParams &p, bool allow_split, int max_cluster, in
     while (wide < p.M && wide < 256) wide *= 2;
     const long long tiles = (long long)((p.N + kTileW - 1) / kTileW) * ((p.M + wide - 1) / wide);
     const long long sms = sm_count(), slots = sms * tc_ctas_per_sm(wide);  // CTAs of one wave
-    if (allow_split && wide <= 128 && 2 * tiles <= sms && ktiles >= 2) {
+    const bool long_k = ktiles >= 128 && 4 * tiles <= slots;
+    if (allow_split && (wide <= 128 || long_k) && 2 * tiles <= sms && ktiles >= 2) {
         int ks = (int)(slots / tiles);
         if (ks > ktiles) ks = ktiles;
         if (ks > max_cluster) ks = max_cluster;
