@@ -405,9 +405,12 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, int rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
     return r;
 }
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
     return v;
 }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiWarps * 32) : "memory"); }
@@ -652,29 +655,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // CTA's partial tile alive until all have read it
         cluster_sync_all();
         if (warp >= 2) {
-            const int row = (warp & 3) * 32 + lane, et = threadIdx.x - 64;
+            // thread et adds weight rows r4 .. r4 + 3 (one 16-byte load per
+            // split) of input rows jo, jo + 4, ...: four rows of the tile per
+            // pass of the 128 threads
+            const int et = threadIdx.x - 64, r4 = (et & 31) * 4, jo = et >> 5;
             const int z = (int)cluster_rank();
             const int per = (tn + sc.ksplit - 1) / sc.ksplit;
             const int j0 = min(tn, z * per), j1 = min(tn, j0 + per);
             int t, n0, m0, kb, nk;
             sc.unit(blockIdx.x, tn, t, n0, m0, kb, nk);
-            const int n = n0 + row;
-            const float brow = p.bias && n < p.N ? ldf(reinterpret_cast<const T *>(p.bias), n) : 0.f;
+            float brow[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int n = n0 + r4 + i;
+                brow[i] = p.bias && n < p.N ? ldf(reinterpret_cast<const T *>(p.bias), n) : 0.f;
+            }
             __nv_bfloat16 *S = reinterpret_cast<__nv_bfloat16 *>(smem + (size_t)nst * st_bytes);
             uint32_t pq[kTcMaxCluster];  // each split's partial tile, as a cluster shared address
 #pragma unroll
             for (int q = 0; q < kTcMaxCluster; q++) pq[q] = q < sc.ksplit ? cluster_map(s_u32(smem), q) : 0u;
             for (int jc = j0; jc < j1; jc += kEpiRows) {
                 const int nr = min(kEpiRows, j1 - jc);
-                for (int j = 0; j < nr; j++) {
-                    const uint32_t off = (uint32_t)(((jc + j) * kTileW + row) * 4);
-                    float x[kTcMaxCluster];
+                for (int j = jo; j < nr; j += 4) {
+                    const uint32_t off = (uint32_t)(((jc + j) * kTileW + r4) * 4);
+                    float4 x[kTcMaxCluster];
 #pragma unroll
-                    for (int q = 0; q < kTcMaxCluster; q++) x[q] = q < sc.ksplit ? ld_cluster_f32(pq[q] + off) : 0.f;
-                    float acc = 0.f;
+                    for (int q = 0; q < kTcMaxCluster; q++)
+                        x[q] = q < sc.ksplit ? ld_cluster_f32x4(pq[q] + off) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                    for (int q = 0; q < kTcMaxCluster; q++) acc += x[q];
-                    S[j * kTileW + row] = __float2bfloat16_rn(acc + brow);
+                    for (int q = 0; q < kTcMaxCluster; q++) {  // in split order: the same bits on every run
+                        acc.x += x[q].x;
+                        acc.y += x[q].y;
+                        acc.z += x[q].z;
+                        acc.w += x[q].w;
+                    }
+                    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x + brow[0], acc.y + brow[1]);
+                    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z + brow[2], acc.w + brow[3]);
+                    uint2 pk;
+                    pk.x = *reinterpret_cast<uint32_t *>(&lo);
+                    pk.y = *reinterpret_cast<uint32_t *>(&hi);
+                    *reinterpret_cast<uint2 *>(S + j * kTileW + r4) = pk;
                 }
                 epi_bar();
                 tc_epi_emit<EPI>(p, S, n0, m0 + jc, nr, et, s_key);
