@@ -5,6 +5,7 @@ import ctypes as C
 import os
 import re
 
+import numpy as np
 import pytest
 import torch
 
@@ -99,3 +100,42 @@ def test_no_cpu_fallback():
         ops.add(a.clone(), a, a)
     with pytest.raises(RuntimeError):
         ops.linear(torch.zeros(1, 2), torch.zeros(1, 3), torch.zeros(2, 3))
+
+
+_STUB = r"""
+#include <stddef.h>
+#include <stdint.h>
+/* stands in for the library's entry point: echoes its arguments */
+int wgb_qwen2_infer(void *m, const int64_t *ids, size_t n, int top_k, float top_p, float t, int64_t *next) {
+    *next = ids[n - 1] * 1000003 + (int64_t)n * 7 + top_k * 11 + (int64_t)(top_p * 64) + (int64_t)(t * 4096);
+    return m == (void *)0x10 ? 0 : 3;
+}
+"""
+
+
+def test_infer_one_token_path_marshals_like_the_array_path(tmp_path):
+    """Qwen2.infer passes a one-token call through reused ctypes buffers; the
+    arguments the entry point sees (and the returned token) match those of
+    the numpy-array path, for every int64 id."""
+    import subprocess
+    from wginfer_b200 import qwen2 as Q
+    src, so = tmp_path / "stub.c", tmp_path / "libstub.so"
+    src.write_text(_STUB)
+    subprocess.run(["gcc", "-shared", "-fPIC", "-O2", "-o", str(so), str(src)], check=True)
+    stub = C.CDLL(str(so))
+    res, args = _lib.SIGNATURES["wgb_qwen2_infer"]
+    stub.wgb_qwen2_infer.restype, stub.wgb_qwen2_infer.argtypes = res, args
+    m = Q.Qwen2.__new__(Q.Qwen2)
+    m._l, m.h = stub, C.c_void_p(0x10)
+    m._init_call_buffers()
+    for tok in (0, 7, 151935, -3, (1 << 62) + 5, -(1 << 63), (1 << 63) - 1):
+        for kw in ({}, {"top_k": 3, "top_p": 0.5, "temperature": 0.25}):
+            want = m.infer(np.array([tok], np.int64), **kw)  # the array path
+            assert m.infer([tok], **kw) == want
+            assert m.infer((tok,), **kw) == want
+    assert m.infer([1, 2, 3]) == m.infer(np.array([1, 2, 3]))
+    with pytest.raises(OverflowError):
+        m.infer([1 << 63])
+    m.h = C.c_void_p(0x20)  # a failing status still raises
+    with pytest.raises(RuntimeError):
+        m.infer([5])

@@ -39,8 +39,16 @@ class Qwen2:
         _lib.check(self._l.wgb_qwen2_create(C.byref(meta), device, max_batch, C.byref(h)), "wgb_qwen2_create")
         self.h = h
         self._pinned = torch.empty(max(1, max_batch), dtype=torch.int64).pin_memory()
+        self._init_call_buffers()
         if weights is not None:
             self.load_weights(weights)
+
+    def _init_call_buffers(self) -> None:
+        # one-token infer calls (every decode step) reuse these instead of
+        # building a numpy array per call (about 3.5 us of host time each)
+        self._tok = (C.c_int64 * 1)()
+        self._next = C.c_int64(0)
+        self._next_ref = C.byref(self._next)
 
     def set_weight(self, name: str, t: torch.Tensor, layer: int = -1) -> None:
         t = t.contiguous()
@@ -61,6 +69,12 @@ class Qwen2:
 
     def infer(self, token_ids, top_k=1, top_p=1.0, temperature=1.0) -> int:
         """Model::infer for sequence 0: returns the next token (host int)."""
+        if (type(token_ids) in (list, tuple) and len(token_ids) == 1 and type(token_ids[0]) is int
+                and -(1 << 63) <= token_ids[0] < (1 << 63)):
+            self._tok[0] = token_ids[0]
+            _lib.check(self._l.wgb_qwen2_infer(self.h, self._tok, 1, top_k, top_p, temperature, self._next_ref),
+                       "infer")
+            return self._next.value
         ids = np.ascontiguousarray(np.asarray(token_ids, dtype=np.int64).reshape(-1))
         nxt = C.c_int64(0)
         _lib.check(self._l.wgb_qwen2_infer(self.h, ids.ctypes.data_as(C.c_void_p), ids.size, top_k, top_p,
