@@ -21,7 +21,8 @@ checks the streams), on the same model in the same run.
 
 Extra objects: `roofline` (the weight-streaming GEMV, the dominant kernel),
 `cpu_baseline` (the reference's own CPU build timed on a bounded sample),
-`clocks`, `op_bandwidth`, and at the end of the line `bs64` (64 sequences
+`clocks`, `op_bandwidth`, `prefill` (one GPU: the prompt's prefill on the
+28-layer model, best of 3), and at the end of the line `bs64` (64 sequences
 with 2048-token prompts on the one-layer model, requests split across the
 GPUs: a strong-scaling workload) and `reference_numerics`.
 
@@ -454,6 +455,11 @@ def run_b200(args):
         result["op_bandwidth"] = op_sweep(peak, quick=world > 1)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args.cpu_steps)
+    if rank == 0 and world == 1 and not args.no_prefill:
+        try:
+            result["prefill"] = prefill_only(args.prompt, 3)
+        except Exception as e:  # a side measurement: the decode line is still printed
+            result["prefill"] = {"error": f"{type(e).__name__}: {e}"[:300]}
     if not args.no_bs64:
         result["bs64"] = bs64(args, world, rank, local)
     if ref_leg is not None:
@@ -623,6 +629,8 @@ def main():
     ap.add_argument("--only-prefill", type=int, default=0, metavar="TOKENS",
                     help="print only the time of one prefill of this many tokens (28-layer model, one GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the one-GPU prefill timing of the --prompt tokens (28-layer model)")
     ap.add_argument("--op-probe", choices=["add", "swiglu", "rms_norm", "argmax"], default=None,
                     help="only launch one swept op a few times at >= 64 MB (for an ncu capture)")
     ap.add_argument("--no-reference-numerics", action="store_true",
