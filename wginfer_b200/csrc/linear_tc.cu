@@ -161,11 +161,6 @@ __device__ __forceinline__ int64_t ld_s64_early(const int64_t *p) {
     asm volatile("ld.global.s64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return (int64_t)v;
 }
-__device__ __forceinline__ float2 ld_f2_early(const float2 *p) {
-    float2 v;
-    asm volatile("ld.global.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p) : "memory");
-    return v;
-}
 
 // The epilogue of a chunk of up to 32 input rows runs in two phases through
 // a shared-memory tile S[32][128] of bf16 (input row j, weight row r):
